@@ -1,0 +1,808 @@
+// chm_engine.cu -- C ABI of the Cherimoya B200 engine (see
+// include/cherimoya_b200.h). Host orchestration only: validation, workspace
+// carving, kernel dispatch. No entry point allocates device memory.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "../../include/cherimoya_b200.h"
+#include "chm_kernels.cuh"
+
+using namespace chm;
+
+namespace {
+
+thread_local long long g_launches = 0;
+
+// ---- optional per-launch CUDA-event timing (benchmark instrumentation)
+enum KClass { kKStem = 0, kKStats = 1, kKMlp = 2, kKProfile = 3, kKCount = 4, kKScore = 5,
+              kKOther = 6, kKClasses = 7 };
+struct TimedLaunch {
+  int cls;
+  cudaEvent_t start, stop;
+};
+struct Timing {
+  bool enabled = false;
+  std::vector<TimedLaunch> pending;
+  std::vector<cudaEvent_t> pool;
+  cudaEvent_t get() {
+    if (!pool.empty()) {
+      cudaEvent_t e = pool.back();
+      pool.pop_back();
+      return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+  }
+};
+thread_local Timing g_timing;
+
+// RAII bracket around one kernel launch.
+struct LaunchTimer {
+  TimedLaunch t{};
+  cudaStream_t st;
+  bool on;
+  LaunchTimer(int cls, cudaStream_t s) : st(s), on(g_timing.enabled) {
+    if (!on) return;
+    t.cls = cls;
+    t.start = g_timing.get();
+    t.stop = g_timing.get();
+    cudaEventRecord(t.start, st);
+  }
+  ~LaunchTimer() {
+    if (!on) return;
+    cudaEventRecord(t.stop, st);
+    g_timing.pending.push_back(t);
+  }
+};
+
+constexpr size_t kAlign = 1024;
+size_t align_up(size_t v, size_t a = kAlign) { return (v + a - 1) / a * a; }
+int round64(int v) { return (v + 63) / 64 * 64; }
+
+struct Dims {
+  int C, CP, H, HP, L, T, Lout, n_layers, n_out, n_groups, n_ctl, mode;
+  float rs;
+  int act_bytes() const { return mode == CHM_MODE_BF16 ? 2 : 4; }
+  int n_chunks() const { return (L + kStatsRows - 1) / kStatsRows; }
+};
+
+Dims dims_of(const chm_model_desc* d) {
+  Dims m;
+  m.C = d->n_filters;
+  m.CP = round64(d->n_filters);
+  m.H = d->expansion * d->n_filters;
+  m.HP = round64(m.H);
+  m.L = d->seq_len;
+  m.T = d->trimming;
+  m.Lout = d->seq_len - 2 * d->trimming;
+  m.n_layers = d->n_layers;
+  m.n_out = d->n_outputs;
+  m.n_groups = d->n_groups;
+  m.n_ctl = d->n_control_tracks;
+  m.mode = d->mode;
+  m.rs = d->residual_scale;
+  return m;
+}
+
+// ---- packed weight buffer layout
+struct PackLayout {
+  size_t stem_w, stem_b, layers, layer_stride, l_convw, l_w1, l_w2;
+  size_t head_f, head_fb, head_lw, head_lb, total;
+};
+
+PackLayout pack_layout(const Dims& m) {
+  PackLayout p;
+  size_t o = 0;
+  p.stem_w = o; o = align_up(o + (size_t)m.C * 4 * kStemTaps * 4);
+  p.stem_b = o; o = align_up(o + (size_t)m.C * 4);
+  p.l_convw = 0;
+  p.l_w1 = align_up(3 * (size_t)m.CP * 4);
+  p.l_w2 = align_up(p.l_w1 + (size_t)m.HP * m.CP * 2);
+  p.layer_stride = align_up(p.l_w2 + (size_t)m.CP * m.HP * 2);
+  p.layers = o; o += p.layer_stride * m.n_layers;
+  const size_t cin = (size_t)m.C + m.n_ctl;
+  p.head_f = o; o = align_up(o + (size_t)m.n_out * cin * kHeadTaps * 4);
+  p.head_fb = o; o = align_up(o + (size_t)m.n_out * 4);
+  p.head_lw = o; o = align_up(o + (size_t)m.n_groups * (m.C + (m.n_ctl > 0 ? 1 : 0)) * 4);
+  p.head_lb = o; o = align_up(o + (size_t)m.n_groups * 4);
+  p.total = o;
+  return p;
+}
+
+// ---- forward workspace layout (for `batch` rows)
+struct FwdLayout {
+  size_t status, counters, stats, partials, xa, xb, total;
+};
+
+FwdLayout fwd_layout(const Dims& m, int batch) {
+  FwdLayout f;
+  size_t o = 0;
+  f.status = o; o = align_up(o + 256);
+  f.counters = o; o = align_up(o + (size_t)batch * 4);
+  f.stats = o; o = align_up(o + (size_t)batch * 8);
+  f.partials = o; o = align_up(o + (size_t)batch * m.n_chunks() * 12);
+  const size_t act = (size_t)batch * m.L * m.CP * m.act_bytes();
+  f.xa = o; o = align_up(o + act);
+  f.xb = o; o = align_up(o + act);
+  f.total = o;
+  return f;
+}
+
+int device_sms() {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
+  return sms > 0 ? sms : 148;
+}
+
+int launch_status() {
+  ++g_launches;
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    fprintf(stderr, "cherimoya_b200: launch failed: %s\n", cudaGetErrorString(e));
+    return CHM_ERR_LAUNCH;
+  }
+  return CHM_OK;
+}
+
+#define CHM_TRY(expr)              \
+  do {                             \
+    const int _s = (expr);         \
+    if (_s != CHM_OK) return _s;   \
+  } while (0)
+
+// ---- MLP kernel dispatch over (act_t, CP, HP)
+template <typename act_t, int CP, int HP>
+int launch_mlp_t(const MlpArgs& a, int grid, cudaStream_t st, bool fast) {
+  const int smem = MlpSmem<CP, HP>::kAlloc;
+  LaunchTimer timer(kKMlp, st);
+  if (fast) {
+    auto k = mlp_kernel<act_t, CP, HP, true>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    k<<<grid, 128, smem, st>>>(a);
+  } else {
+    auto k = mlp_kernel<act_t, CP, HP, false>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    k<<<grid, 128, smem, st>>>(a);
+  }
+  return launch_status();
+}
+
+template <typename act_t>
+int launch_mlp(const Dims& m, const MlpArgs& a, int grid, cudaStream_t st) {
+  const bool fast = (m.mode == CHM_MODE_BF16);
+  if (m.CP == 64) {
+    switch (m.HP) {
+      case 64: return launch_mlp_t<act_t, 64, 64>(a, grid, st, fast);
+      case 128: return launch_mlp_t<act_t, 64, 128>(a, grid, st, fast);
+      case 192: return launch_mlp_t<act_t, 64, 192>(a, grid, st, fast);
+      case 256: return launch_mlp_t<act_t, 64, 256>(a, grid, st, fast);
+    }
+  } else if (m.CP == 128) {
+    switch (m.HP) {
+      case 128: return launch_mlp_t<act_t, 128, 128>(a, grid, st, fast);
+      case 192: return launch_mlp_t<act_t, 128, 192>(a, grid, st, fast);
+      case 256: return launch_mlp_t<act_t, 128, 256>(a, grid, st, fast);
+    }
+  }
+  return CHM_ERR_UNSUPPORTED;
+}
+
+template <typename act_t>
+int launch_stats(const Dims& m, const act_t* X, const float* convw, int dil, int batch,
+                 float* partials, unsigned* counters, float2* stats, cudaStream_t st) {
+  dim3 grid(m.n_chunks(), batch);
+  LaunchTimer timer(kKStats, st);
+  if (m.CP == 64) {
+    stats_kernel<act_t, 64><<<grid, 256, 0, st>>>(X, convw, dil, m.L, m.C, 1e-3f, partials,
+                                                  counters, stats);
+  } else if (m.CP == 128) {
+    stats_kernel<act_t, 128><<<grid, 256, 0, st>>>(X, convw, dil, m.L, m.C, 1e-3f, partials,
+                                                   counters, stats);
+  } else {
+    return CHM_ERR_UNSUPPORTED;
+  }
+  return launch_status();
+}
+
+// The whole forward for `batch` rows whose stem input is `in` (kind kIn).
+template <typename act_t>
+int run_forward_t(const Dims& m, const PackLayout& pl, const uint8_t* packed, int batch, int kIn,
+                  const StemInput& in, const float* x_ctl, float* profile, float* logcounts,
+                  uint8_t* ws, cudaStream_t st) {
+  const FwdLayout f = fwd_layout(m, batch);
+  unsigned* counters = reinterpret_cast<unsigned*>(ws + f.counters);
+  float2* stats = reinterpret_cast<float2*>(ws + f.stats);
+  float* partials = reinterpret_cast<float*>(ws + f.partials);
+  int* status = reinterpret_cast<int*>(ws + f.status);
+  act_t* xa = reinterpret_cast<act_t*>(ws + f.xa);
+  act_t* xb = reinterpret_cast<act_t*>(ws + f.xb);
+  if (cudaMemsetAsync(counters, 0, (size_t)batch * 4, st) != cudaSuccess) return CHM_ERR_CUDA;
+
+  // stem
+  {
+    dim3 grid((m.L + kStemL - 1) / kStemL, batch);
+    const float* w = reinterpret_cast<const float*>(packed + pl.stem_w);
+    const float* bias = reinterpret_cast<const float*>(packed + pl.stem_b);
+    LaunchTimer timer(kKStem, st);
+    if (kIn == kInDense)
+      stem_kernel<act_t, kInDense><<<grid, m.CP, 0, st>>>(in, w, bias, xa, m.L, m.C, m.CP);
+    else if (kIn == kInBases)
+      stem_kernel<act_t, kInBases><<<grid, m.CP, 0, st>>>(in, w, bias, xa, m.L, m.C, m.CP);
+    else
+      stem_kernel<act_t, kInIsm><<<grid, m.CP, 0, st>>>(in, w, bias, xa, m.L, m.C, m.CP);
+    CHM_TRY(launch_status());
+  }
+  // block stack
+  const long long rows = (long long)batch * m.L;
+  const int n_tiles = static_cast<int>((rows + kTileRows - 1) / kTileRows);
+  const int grid = std::min(n_tiles, device_sms());
+  for (int i = 0; i < m.n_layers; ++i) {
+    const uint8_t* lw = packed + pl.layers + pl.layer_stride * i;
+    const float* convw = reinterpret_cast<const float*>(lw + pl.l_convw);
+    const int dil = 1 << i;
+    CHM_TRY(launch_stats<act_t>(m, xa, convw, dil, batch, partials, counters, stats, st));
+    MlpArgs a;
+    a.X_in = xa;
+    a.X_out = xb;
+    a.stats = stats;
+    a.w1 = lw + pl.l_w1;
+    a.w2 = lw + pl.l_w2;
+    a.convw = convw;
+    a.dil = dil;
+    a.L = m.L;
+    a.C = m.C;
+    a.rows = rows;
+    a.n_tiles = n_tiles;
+    a.status = status;
+    CHM_TRY(launch_mlp<act_t>(m, a, grid, st));
+    std::swap(xa, xb);
+  }
+  // heads
+  {
+    const int cin = m.C + m.n_ctl;
+    const int smem = (cin * kHeadWin + kHeadWarps * kHeadJ) * 4;
+    auto k = profile_head_kernel<act_t>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    dim3 grid_h((m.Lout + kHeadJ - 1) / kHeadJ, batch);
+    {
+    LaunchTimer timer(kKProfile, st);
+    k<<<grid_h, kHeadWarps * 32, smem, st>>>(
+        xa, x_ctl, reinterpret_cast<const float*>(packed + pl.head_f),
+        reinterpret_cast<const float*>(packed + pl.head_fb), profile, m.L, m.C, m.CP, m.n_ctl,
+        m.n_out, m.T, m.Lout);
+    }
+    CHM_TRY(launch_status());
+    {
+    LaunchTimer timer(kKCount, st);
+    count_head_kernel<act_t><<<batch, 256, 0, st>>>(
+        xa, x_ctl, reinterpret_cast<const float*>(packed + pl.head_lw),
+        reinterpret_cast<const float*>(packed + pl.head_lb), logcounts, m.L, m.C, m.CP, m.n_ctl,
+        m.n_groups, m.T);
+    }
+    CHM_TRY(launch_status());
+  }
+  return CHM_OK;
+}
+
+int run_forward(const Dims& m, const uint8_t* packed, int batch, int kIn, const StemInput& in,
+                const float* x_ctl, float* profile, float* logcounts, uint8_t* ws,
+                cudaStream_t st) {
+  const PackLayout pl = pack_layout(m);
+  if (m.mode == CHM_MODE_BF16)
+    return run_forward_t<__nv_bfloat16>(m, pl, packed, batch, kIn, in, x_ctl, profile, logcounts,
+                                        ws, st);
+  return run_forward_t<float>(m, pl, packed, batch, kIn, in, x_ctl, profile, logcounts, ws, st);
+}
+
+int validate(const chm_model_desc* d) {
+  if (!d) return CHM_ERR_INVALID_ARGUMENT;
+  if (d->n_filters < 1 || d->n_layers < 0 || d->n_layers > 24 || d->expansion < 1 ||
+      d->n_outputs < 1 || d->n_groups < 1 || d->n_control_tracks < 0 || d->trimming < 0 ||
+      d->seq_len < 1)
+    return CHM_ERR_INVALID_ARGUMENT;
+  if (d->mode != CHM_MODE_FP32 && d->mode != CHM_MODE_BF16) return CHM_ERR_INVALID_ARGUMENT;
+  if (d->seq_len - 2 * d->trimming < 1) return CHM_ERR_UNSUPPORTED;
+  const Dims m = dims_of(d);
+  if (m.CP > 128 || m.HP > 256) return CHM_ERR_UNSUPPORTED;
+  const int cin = m.C + m.n_ctl;
+  if ((cin * kHeadWin + kHeadWarps * kHeadJ) * 4 > 227 * 1024) return CHM_ERR_UNSUPPORTED;
+  return CHM_OK;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+size_t ism_len(const Dims& m) { return (size_t)m.n_out * m.Lout; }
+
+struct IsmLayout {
+  size_t fwd, ref_prof, ref_prob, ref_lc, mut_prof, mut_lc, total;
+};
+
+IsmLayout ism_layout(const Dims& m, int n_seqs, int mb) {
+  IsmLayout l;
+  size_t o = 0;
+  l.fwd = o; o = align_up(o + fwd_layout(m, std::max(n_seqs, mb)).total);
+  l.ref_prof = o; o = align_up(o + (size_t)n_seqs * ism_len(m) * 4);
+  l.ref_prob = o; o = align_up(o + (size_t)n_seqs * ism_len(m) * 4);
+  l.ref_lc = o; o = align_up(o + (size_t)n_seqs * m.n_groups * 4);
+  l.mut_prof = o; o = align_up(o + (size_t)mb * ism_len(m) * 4);
+  l.mut_lc = o; o = align_up(o + (size_t)mb * m.n_groups * 4);
+  l.total = o;
+  return l;
+}
+
+constexpr int kVariantChunk = 1024;
+
+struct VarLayout {
+  size_t fwd, ref_prof, ref_prob, ref_lc, alt_prof, alt_lc, total;
+  int chunk;
+};
+
+VarLayout var_layout(const Dims& m, int n_pairs) {
+  VarLayout l;
+  l.chunk = std::max(1, std::min(n_pairs, kVariantChunk));
+  size_t o = 0;
+  l.fwd = o; o = align_up(o + fwd_layout(m, l.chunk).total);
+  l.ref_prof = o; o = align_up(o + (size_t)l.chunk * ism_len(m) * 4);
+  l.ref_prob = o; o = align_up(o + (size_t)l.chunk * ism_len(m) * 4);
+  l.ref_lc = o; o = align_up(o + (size_t)l.chunk * m.n_groups * 4);
+  l.alt_prof = o; o = align_up(o + (size_t)l.chunk * ism_len(m) * 4);
+  l.alt_lc = o; o = align_up(o + (size_t)l.chunk * m.n_groups * 4);
+  l.total = o;
+  return l;
+}
+
+Dims block_dims(int C, int H, int x_dtype) {
+  Dims m{};
+  m.C = C;
+  m.CP = round64(C);
+  m.H = H;
+  m.HP = round64(H);
+  m.mode = (x_dtype == CHM_INPUT_BF16) ? CHM_MODE_BF16 : CHM_MODE_FP32;
+  m.rs = 1.f;
+  return m;
+}
+
+bool block_supported(int C, int H) {
+  return C >= 1 && H >= C && round64(C) <= 128 && round64(H) <= 256;
+}
+
+struct BlockWsLayout {
+  size_t status, counters, stats, partials, xin, xout, total;
+};
+
+BlockWsLayout block_ws_layout(const Dims& m, int batch) {
+  BlockWsLayout b;
+  size_t o = 0;
+  b.status = o; o = align_up(o + 256);
+  b.counters = o; o = align_up(o + (size_t)batch * 4);
+  b.stats = o; o = align_up(o + (size_t)batch * 8);
+  b.partials = o; o = align_up(o + (size_t)batch * m.n_chunks() * 12);
+  const size_t act = (m.C == m.CP) ? 0 : (size_t)batch * m.L * m.CP * m.act_bytes();
+  b.xin = o; o = align_up(o + act);
+  b.xout = o; o = align_up(o + act);
+  b.total = o;
+  return b;
+}
+
+template <typename act_t>
+int run_block_t(const Dims& m, int batch, int dil, const uint8_t* packed, const act_t* x,
+                act_t* out, uint8_t* ws, cudaStream_t st) {
+  const BlockWsLayout bl = block_ws_layout(m, batch);
+  const PackLayout pl = pack_layout(m);
+  unsigned* counters = reinterpret_cast<unsigned*>(ws + bl.counters);
+  float2* stats = reinterpret_cast<float2*>(ws + bl.stats);
+  float* partials = reinterpret_cast<float*>(ws + bl.partials);
+  const long long rows = (long long)batch * m.L;
+  const act_t* xin = x;
+  act_t* xout = out;
+  if (m.C != m.CP) {
+    act_t* pin = reinterpret_cast<act_t*>(ws + bl.xin);
+    pad_channels_kernel<act_t><<<(unsigned)((rows * m.CP + 255) / 256), 256, 0, st>>>(
+        x, pin, rows, m.C, m.CP);
+    CHM_TRY(launch_status());
+    xin = pin;
+    xout = reinterpret_cast<act_t*>(ws + bl.xout);
+  }
+  if (cudaMemsetAsync(counters, 0, (size_t)batch * 4, st) != cudaSuccess) return CHM_ERR_CUDA;
+  const float* convw = reinterpret_cast<const float*>(packed + pl.l_convw);
+  CHM_TRY(launch_stats<act_t>(m, xin, convw, dil, batch, partials, counters, stats, st));
+  const int n_tiles = static_cast<int>((rows + kTileRows - 1) / kTileRows);
+  MlpArgs a;
+  a.X_in = xin;
+  a.X_out = xout;
+  a.stats = stats;
+  a.w1 = packed + pl.l_w1;
+  a.w2 = packed + pl.l_w2;
+  a.convw = convw;
+  a.dil = dil;
+  a.L = m.L;
+  a.C = m.C;
+  a.rows = rows;
+  a.n_tiles = n_tiles;
+  a.status = reinterpret_cast<int*>(ws + bl.status);
+  CHM_TRY(launch_mlp<act_t>(m, a, std::min(n_tiles, device_sms()), st));
+  if (m.C != m.CP) {
+    unpad_channels_kernel<act_t><<<(unsigned)((rows * m.C + 255) / 256), 256, 0, st>>>(
+        xout, out, rows, m.C, m.CP);
+    CHM_TRY(launch_status());
+  }
+  return CHM_OK;
+}
+
+}  // namespace
+
+// ====================================================================== ABI
+extern "C" {
+
+int32_t chm_abi_version(void) { return CHM_ABI_VERSION; }
+
+const char* chm_error_string(int32_t s) {
+  switch (s) {
+    case CHM_OK: return "ok";
+    case CHM_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case CHM_ERR_UNSUPPORTED: return "unsupported model configuration";
+    case CHM_ERR_WORKSPACE: return "workspace or packed-weight buffer too small or misaligned";
+    case CHM_ERR_LAUNCH: return "kernel launch failed";
+    case CHM_ERR_DEVICE_TIMEOUT: return "a bounded device-side wait timed out";
+    case CHM_ERR_CUDA: return "CUDA runtime error";
+  }
+  return "unknown status";
+}
+
+int32_t chm_validate(const chm_model_desc* desc) { return validate(desc); }
+
+size_t chm_packed_weights_bytes(const chm_model_desc* desc) {
+  if (validate(desc) != CHM_OK) return 0;
+  return pack_layout(dims_of(desc)).total;
+}
+
+int32_t chm_pack_weights(const chm_model_desc* desc, const chm_params* p, void* packed,
+                         size_t packed_bytes, chm_stream_t stream) {
+  g_launches = 0;
+  CHM_TRY(validate(desc));
+  if (!p || !packed || !p->iconv_weight || !p->iconv_bias || !p->fconv_weight ||
+      !p->fconv_bias || !p->linear_weight || !p->linear_bias)
+    return CHM_ERR_INVALID_ARGUMENT;
+  if (desc->n_layers > 0 && (!p->conv_weight || !p->linear1_weight || !p->linear2_weight))
+    return CHM_ERR_INVALID_ARGUMENT;
+  const Dims m = dims_of(desc);
+  const PackLayout pl = pack_layout(m);
+  if (packed_bytes < pl.total || !aligned(packed, kAlign)) return CHM_ERR_WORKSPACE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* dst = static_cast<uint8_t*>(packed);
+  auto copy = [&](const float* src, size_t off, long long n) -> int {
+    copy_f32_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
+        src, reinterpret_cast<float*>(dst + off), n);
+    return launch_status();
+  };
+  CHM_TRY(copy(p->iconv_weight, pl.stem_w, (long long)m.C * 4 * kStemTaps));
+  CHM_TRY(copy(p->iconv_bias, pl.stem_b, m.C));
+  for (int i = 0; i < m.n_layers; ++i) {
+    if (!p->conv_weight[i] || !p->linear1_weight[i] || !p->linear2_weight[i])
+      return CHM_ERR_INVALID_ARGUMENT;
+    uint8_t* lw = dst + pl.layers + pl.layer_stride * i;
+    pack_convw_kernel<<<(3 * m.CP + 255) / 256, 256, 0, st>>>(
+        p->conv_weight[i], m.C, m.CP, reinterpret_cast<float*>(lw + pl.l_convw));
+    CHM_TRY(launch_status());
+    pack_sw128_kernel<<<(m.HP * m.CP + 255) / 256, 256, 0, st>>>(
+        p->linear1_weight[i], m.H, m.C, m.HP, m.CP, 1.0f, lw + pl.l_w1);
+    CHM_TRY(launch_status());
+    // residual_scale folded into linear2 before the bf16 cast
+    // (upstream cheri.py:1021-1024)
+    pack_sw128_kernel<<<(m.CP * m.HP + 255) / 256, 256, 0, st>>>(
+        p->linear2_weight[i], m.C, m.H, m.CP, m.HP, m.rs, lw + pl.l_w2);
+    CHM_TRY(launch_status());
+  }
+  const long long cin = (long long)m.C + m.n_ctl;
+  CHM_TRY(copy(p->fconv_weight, pl.head_f, (long long)m.n_out * cin * kHeadTaps));
+  CHM_TRY(copy(p->fconv_bias, pl.head_fb, m.n_out));
+  CHM_TRY(copy(p->linear_weight, pl.head_lw,
+               (long long)m.n_groups * (m.C + (m.n_ctl > 0 ? 1 : 0))));
+  CHM_TRY(copy(p->linear_bias, pl.head_lb, m.n_groups));
+  return CHM_OK;
+}
+
+size_t chm_forward_workspace_bytes(const chm_model_desc* desc, int32_t batch) {
+  if (validate(desc) != CHM_OK || batch < 1) return 0;
+  return fwd_layout(dims_of(desc), batch).total;
+}
+
+static int forward_common(const chm_model_desc* desc, const void* packed, int32_t batch, int kIn,
+                          const StemInput& in, const float* x_ctl, float* profile,
+                          float* logcounts, void* ws, size_t ws_bytes, chm_stream_t stream) {
+  g_launches = 0;
+  CHM_TRY(validate(desc));
+  if (batch < 0 || !packed || !profile || !logcounts || !ws) return CHM_ERR_INVALID_ARGUMENT;
+  if (batch == 0) return CHM_OK;
+  if (desc->n_control_tracks > 0 && !x_ctl) return CHM_ERR_INVALID_ARGUMENT;
+  const Dims m = dims_of(desc);
+  if (ws_bytes < fwd_layout(m, batch).total || !aligned(ws, kAlign) || !aligned(packed, kAlign))
+    return CHM_ERR_WORKSPACE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(ws, 0, sizeof(int), st) != cudaSuccess) return CHM_ERR_CUDA;
+  return run_forward(m, static_cast<const uint8_t*>(packed), batch, kIn, in, x_ctl, profile,
+                     logcounts, static_cast<uint8_t*>(ws), st);
+}
+
+int32_t chm_forward(const chm_model_desc* desc, const void* packed, int32_t batch, const void* x,
+                    int32_t input_dtype, const float* x_ctl, float* profile, float* logcounts,
+                    void* workspace, size_t workspace_bytes, chm_stream_t stream) {
+  if (!x && batch > 0) return CHM_ERR_INVALID_ARGUMENT;
+  if (input_dtype != CHM_INPUT_F32 && input_dtype != CHM_INPUT_BF16)
+    return CHM_ERR_INVALID_ARGUMENT;
+  StemInput in{};
+  in.x = x;
+  in.x_bf16 = (input_dtype == CHM_INPUT_BF16);
+  return forward_common(desc, packed, batch, kInDense, in, x_ctl, profile, logcounts, workspace,
+                        workspace_bytes, stream);
+}
+
+int32_t chm_forward_bases(const chm_model_desc* desc, const void* packed, int32_t batch,
+                          const int8_t* bases, const float* x_ctl, float* profile,
+                          float* logcounts, void* workspace, size_t workspace_bytes,
+                          chm_stream_t stream) {
+  if (!bases && batch > 0) return CHM_ERR_INVALID_ARGUMENT;
+  StemInput in{};
+  in.bases = bases;
+  return forward_common(desc, packed, batch, kInBases, in, x_ctl, profile, logcounts, workspace,
+                        workspace_bytes, stream);
+}
+
+size_t chm_ism_workspace_bytes(const chm_model_desc* desc, int32_t n_seqs, int32_t mutant_batch) {
+  if (validate(desc) != CHM_OK || n_seqs < 1 || mutant_batch < 1) return 0;
+  return ism_layout(dims_of(desc), n_seqs, mutant_batch).total;
+}
+
+int32_t chm_ism(const chm_model_desc* desc, const void* packed, int32_t n_seqs,
+                const int8_t* bases, int32_t start, int32_t end, int32_t mutant_batch,
+                float* d_logcount, float* jsd, void* workspace, size_t workspace_bytes,
+                chm_stream_t stream) {
+  CHM_TRY(validate(desc));
+  if (n_seqs < 0 || !packed || !bases || !d_logcount || !jsd || !workspace || mutant_batch < 1)
+    return CHM_ERR_INVALID_ARGUMENT;
+  if (n_seqs == 0) return CHM_OK;
+  if (desc->n_control_tracks > 0) return CHM_ERR_UNSUPPORTED;
+  if (start < 0 || end > desc->seq_len || end <= start) return CHM_ERR_INVALID_ARGUMENT;
+  const Dims m = dims_of(desc);
+  const IsmLayout il = ism_layout(m, n_seqs, mutant_batch);
+  if (workspace_bytes < il.total || !aligned(workspace, kAlign) || !aligned(packed, kAlign))
+    return CHM_ERR_WORKSPACE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const uint8_t* pk = static_cast<const uint8_t*>(packed);
+  float* ref_prof = reinterpret_cast<float*>(ws + il.ref_prof);
+  float* ref_prob = reinterpret_cast<float*>(ws + il.ref_prob);
+  float* ref_lc = reinterpret_cast<float*>(ws + il.ref_lc);
+  float* mut_prof = reinterpret_cast<float*>(ws + il.mut_prof);
+  float* mut_lc = reinterpret_cast<float*>(ws + il.mut_lc);
+  uint8_t* fws = ws + il.fwd;
+  long long launches = 0;
+  if (cudaMemsetAsync(ws, 0, sizeof(int), st) != cudaSuccess) return CHM_ERR_CUDA;
+
+  StemInput rin{};
+  rin.bases = bases;
+  g_launches = 0;
+  CHM_TRY(run_forward(m, pk, n_seqs, kInBases, rin, nullptr, ref_prof, ref_lc, fws, st));
+  launches += g_launches;
+  const int len = static_cast<int>(ism_len(m));
+  softmax_rows_kernel<<<n_seqs, 256, 0, st>>>(ref_prof, ref_prob, len);
+  CHM_TRY(launch_status());
+  const int W = end - start;
+  const long long total = (long long)n_seqs * W * 3;
+  for (long long m0 = 0; m0 < total; m0 += mutant_batch) {
+    const int nb = static_cast<int>(std::min<long long>(mutant_batch, total - m0));
+    StemInput min{};
+    min.bases = bases;
+    min.mut0 = m0;
+    min.ism_start = start;
+    min.ism_width = W;
+    g_launches = 0;
+    CHM_TRY(run_forward(m, pk, nb, kInIsm, min, nullptr, mut_prof, mut_lc, fws, st));
+    launches += g_launches;
+    ScoreArgs sa{};
+    sa.logits = mut_prof;
+    sa.ref_probs = ref_prob;
+    sa.lc = mut_lc;
+    sa.lc_ref = ref_lc;
+    sa.len = len;
+    sa.n_groups = m.n_groups;
+    sa.mut0 = m0;
+    sa.per_ref = 3 * W;
+    sa.ism = 1;
+    sa.ism_start = start;
+    sa.ism_width = W;
+    sa.bases = bases;
+    sa.L = m.L;
+    sa.d_logcount = d_logcount;
+    sa.jsd = jsd;
+    {
+      LaunchTimer timer(kKScore, st);
+      score_kernel<<<nb, 256, 0, st>>>(sa);
+    }
+    CHM_TRY(launch_status());
+    ++launches;
+  }
+  {
+    const long long n = (long long)n_seqs * W;
+    ism_fill_ref_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(bases, m.L, start, W,
+                                                                     m.n_groups, n_seqs,
+                                                                     d_logcount, jsd);
+    CHM_TRY(launch_status());
+    launches += 2;
+  }
+  g_launches = launches;
+  return CHM_OK;
+}
+
+size_t chm_variant_workspace_bytes(const chm_model_desc* desc, int32_t n_pairs) {
+  if (validate(desc) != CHM_OK || n_pairs < 1) return 0;
+  return var_layout(dims_of(desc), n_pairs).total;
+}
+
+int32_t chm_variant(const chm_model_desc* desc, const void* packed, int32_t n_pairs,
+                    const int8_t* ref_bases, const int8_t* alt_bases, float* d_logcount,
+                    float* jsd, void* workspace, size_t workspace_bytes, chm_stream_t stream) {
+  CHM_TRY(validate(desc));
+  if (n_pairs < 0 || !packed || !ref_bases || !alt_bases || !d_logcount || !jsd || !workspace)
+    return CHM_ERR_INVALID_ARGUMENT;
+  if (n_pairs == 0) return CHM_OK;
+  if (desc->n_control_tracks > 0) return CHM_ERR_UNSUPPORTED;
+  const Dims m = dims_of(desc);
+  const VarLayout vl = var_layout(m, n_pairs);
+  if (workspace_bytes < vl.total || !aligned(workspace, kAlign) || !aligned(packed, kAlign))
+    return CHM_ERR_WORKSPACE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const uint8_t* pk = static_cast<const uint8_t*>(packed);
+  float* ref_prof = reinterpret_cast<float*>(ws + vl.ref_prof);
+  float* ref_prob = reinterpret_cast<float*>(ws + vl.ref_prob);
+  float* ref_lc = reinterpret_cast<float*>(ws + vl.ref_lc);
+  float* alt_prof = reinterpret_cast<float*>(ws + vl.alt_prof);
+  float* alt_lc = reinterpret_cast<float*>(ws + vl.alt_lc);
+  uint8_t* fws = ws + vl.fwd;
+  const int len = static_cast<int>(ism_len(m));
+  long long launches = 0;
+  if (cudaMemsetAsync(ws, 0, sizeof(int), st) != cudaSuccess) return CHM_ERR_CUDA;
+  for (int p0 = 0; p0 < n_pairs; p0 += vl.chunk) {
+    const int nb = std::min(vl.chunk, n_pairs - p0);
+    StemInput rin{};
+    rin.bases = ref_bases + (long long)p0 * m.L;
+    g_launches = 0;
+    CHM_TRY(run_forward(m, pk, nb, kInBases, rin, nullptr, ref_prof, ref_lc, fws, st));
+    launches += g_launches;
+    StemInput ain{};
+    ain.bases = alt_bases + (long long)p0 * m.L;
+    g_launches = 0;
+    CHM_TRY(run_forward(m, pk, nb, kInBases, ain, nullptr, alt_prof, alt_lc, fws, st));
+    launches += g_launches;
+    softmax_rows_kernel<<<nb, 256, 0, st>>>(ref_prof, ref_prob, len);
+    CHM_TRY(launch_status());
+    ScoreArgs sa{};
+    sa.logits = alt_prof;
+    sa.ref_probs = ref_prob;
+    sa.lc = alt_lc;
+    sa.lc_ref = ref_lc;
+    sa.len = len;
+    sa.n_groups = m.n_groups;
+    sa.mut0 = 0;
+    sa.per_ref = 1;
+    sa.ism = 0;
+    sa.d_logcount = d_logcount + (long long)p0 * m.n_groups;
+    sa.jsd = jsd + p0;
+    score_kernel<<<nb, 256, 0, st>>>(sa);
+    CHM_TRY(launch_status());
+    launches += 2;
+  }
+  g_launches = launches;
+  return CHM_OK;
+}
+
+size_t chm_block_packed_bytes(int32_t n_filters, int32_t hidden) {
+  if (!block_supported(n_filters, hidden)) return 0;
+  const Dims m = block_dims(n_filters, hidden, CHM_INPUT_F32);
+  return pack_layout(m).layer_stride;
+}
+
+int32_t chm_pack_block(int32_t n_filters, int32_t hidden, float residual_scale,
+                       const float* conv_weight, const float* linear1_weight,
+                       const float* linear2_weight, void* packed, size_t packed_bytes,
+                       chm_stream_t stream) {
+  g_launches = 0;
+  if (!block_supported(n_filters, hidden)) return CHM_ERR_UNSUPPORTED;
+  if (!conv_weight || !linear1_weight || !linear2_weight || !packed)
+    return CHM_ERR_INVALID_ARGUMENT;
+  const Dims m = block_dims(n_filters, hidden, CHM_INPUT_F32);
+  const PackLayout pl = pack_layout(m);
+  if (packed_bytes < pl.layer_stride || !aligned(packed, kAlign)) return CHM_ERR_WORKSPACE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* lw = static_cast<uint8_t*>(packed);
+  pack_convw_kernel<<<(3 * m.CP + 255) / 256, 256, 0, st>>>(
+      conv_weight, m.C, m.CP, reinterpret_cast<float*>(lw + pl.l_convw));
+  CHM_TRY(launch_status());
+  pack_sw128_kernel<<<(m.HP * m.CP + 255) / 256, 256, 0, st>>>(linear1_weight, m.H, m.C, m.HP,
+                                                               m.CP, 1.0f, lw + pl.l_w1);
+  CHM_TRY(launch_status());
+  pack_sw128_kernel<<<(m.CP * m.HP + 255) / 256, 256, 0, st>>>(
+      linear2_weight, m.C, m.H, m.CP, m.HP, residual_scale, lw + pl.l_w2);
+  return launch_status();
+}
+
+size_t chm_block_workspace_bytes(int32_t batch, int32_t seq_len, int32_t n_filters,
+                                 int32_t x_dtype) {
+  if (batch < 1 || seq_len < 1 || n_filters < 1 || round64(n_filters) > 128) return 0;
+  Dims m = block_dims(n_filters, n_filters, x_dtype);
+  m.L = seq_len;
+  return block_ws_layout(m, batch).total;
+}
+
+int32_t chm_block_forward(int32_t batch, int32_t seq_len, int32_t n_filters, int32_t hidden,
+                          int32_t dilation, int32_t x_dtype, const void* packed, const void* x,
+                          void* out, void* workspace, size_t workspace_bytes,
+                          chm_stream_t stream) {
+  g_launches = 0;
+  if (!block_supported(n_filters, hidden)) return CHM_ERR_UNSUPPORTED;
+  if (batch < 0 || seq_len < 1 || dilation < 0 || !packed || !workspace ||
+      (x_dtype != CHM_INPUT_F32 && x_dtype != CHM_INPUT_BF16))
+    return CHM_ERR_INVALID_ARGUMENT;
+  if (batch == 0) return CHM_OK;
+  if (!x || !out || x == out) return CHM_ERR_INVALID_ARGUMENT;
+  Dims m = block_dims(n_filters, hidden, x_dtype);
+  m.L = seq_len;
+  if (workspace_bytes < block_ws_layout(m, batch).total || !aligned(workspace, kAlign) ||
+      !aligned(packed, kAlign) || !aligned(x, 16) || !aligned(out, 16))
+    return CHM_ERR_WORKSPACE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (cudaMemsetAsync(ws, 0, sizeof(int), st) != cudaSuccess) return CHM_ERR_CUDA;
+  const uint8_t* pk = static_cast<const uint8_t*>(packed);
+  if (x_dtype == CHM_INPUT_BF16)
+    return run_block_t<__nv_bfloat16>(m, batch, dilation, pk,
+                                      static_cast<const __nv_bfloat16*>(x),
+                                      static_cast<__nv_bfloat16*>(out), ws, st);
+  return run_block_t<float>(m, batch, dilation, pk, static_cast<const float*>(x),
+                            static_cast<float*>(out), ws, st);
+}
+
+int32_t chm_read_status(void* workspace, chm_stream_t stream) {
+  if (!workspace) return CHM_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaStreamSynchronize(st) != cudaSuccess) return CHM_ERR_CUDA;
+  int s = 0;
+  if (cudaMemcpy(&s, workspace, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return CHM_ERR_CUDA;
+  if (s != 0 && cudaMemset(workspace, 0, sizeof(int)) != cudaSuccess) return CHM_ERR_CUDA;
+  return s;
+}
+
+int64_t chm_last_launch_count(void) { return g_launches; }
+
+void chm_timing_enable(int32_t enable) { g_timing.enabled = (enable != 0); }
+
+int32_t chm_timing_collect(double* ms_per_class, int64_t* launches_per_class) {
+  for (int c = 0; c < kKClasses; ++c) {
+    if (ms_per_class) ms_per_class[c] = 0.0;
+    if (launches_per_class) launches_per_class[c] = 0;
+  }
+  int status = CHM_OK;
+  for (TimedLaunch& t : g_timing.pending) {
+    float ms = 0.f;
+    if (cudaEventSynchronize(t.stop) != cudaSuccess ||
+        cudaEventElapsedTime(&ms, t.start, t.stop) != cudaSuccess)
+      status = CHM_ERR_CUDA;
+    if (ms_per_class) ms_per_class[t.cls] += ms;
+    if (launches_per_class) launches_per_class[t.cls] += 1;
+    g_timing.pool.push_back(t.start);
+    g_timing.pool.push_back(t.stop);
+  }
+  g_timing.pending.clear();
+  return status;
+}
+
+}  // extern "C"

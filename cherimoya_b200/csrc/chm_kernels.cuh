@@ -1,0 +1,841 @@
+// chm_kernels.cuh -- device kernels of the Cherimoya B200 engine.
+//
+// Activation layout in HBM: the residual stream of a batch is one row-major
+// matrix X[(n * L + l) * CP + c] (NLC, channels innermost, padded to CP, a
+// multiple of 64; padded channels hold 0). act_t is float (fp32 mode) or
+// __nv_bfloat16 (bf16 mode).
+#pragma once
+#include <cuda_bf16.h>
+#include <cstdint>
+
+#include "chm_ptx.cuh"
+
+namespace chm {
+
+constexpr int kStemTaps = 21;   // iconv kernel size (upstream cherimoya.py:173)
+constexpr int kStemPad = 10;
+constexpr int kHeadTaps = 75;   // fconv kernel size (upstream cherimoya.py:182-184)
+constexpr int kHeadPad = 37;
+constexpr int kTileRows = 128;  // MMA M
+constexpr int kStatsRows = 128; // rows per LayerNorm-statistics partial
+
+enum : int { kStatusOk = 0, kStatusTimeout = 5 };
+
+template <typename T> __device__ __forceinline__ float to_f32(T v);
+template <> __device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+template <typename T> __device__ __forceinline__ T from_f32(float v);
+template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+// Loads / stores of `N` consecutive activations (N * sizeof(act_t) is 4, 8
+// or 16 bytes and the address is aligned to it).
+template <typename T, int N> struct Vec;
+template <int N> struct Vec<float, N> {
+  static __device__ __forceinline__ void load(const float* p, float (&v)[N]) {
+    if constexpr (N == 4) {
+      float4 t = *reinterpret_cast<const float4*>(p);
+      v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+    } else if constexpr (N == 2) {
+      float2 t = *reinterpret_cast<const float2*>(p);
+      v[0] = t.x; v[1] = t.y;
+    } else {
+#pragma unroll
+      for (int i = 0; i < N; ++i) v[i] = p[i];
+    }
+  }
+  static __device__ __forceinline__ void store(float* p, const float (&v)[N]) {
+    if constexpr (N == 4) {
+      *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    } else if constexpr (N == 2) {
+      *reinterpret_cast<float2*>(p) = make_float2(v[0], v[1]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < N; ++i) p[i] = v[i];
+    }
+  }
+};
+template <int N> struct Vec<__nv_bfloat16, N> {
+  static __device__ __forceinline__ void load(const __nv_bfloat16* p, float (&v)[N]) {
+    if constexpr (N == 4) {
+      uint2 t = *reinterpret_cast<const uint2*>(p);
+      __nv_bfloat162 a = *reinterpret_cast<__nv_bfloat162*>(&t.x);
+      __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&t.y);
+      float2 fa = __bfloat1622float2(a), fb = __bfloat1622float2(b);
+      v[0] = fa.x; v[1] = fa.y; v[2] = fb.x; v[3] = fb.y;
+    } else if constexpr (N == 2) {
+      __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(p);
+      float2 fa = __bfloat1622float2(a);
+      v[0] = fa.x; v[1] = fa.y;
+    } else {
+#pragma unroll
+      for (int i = 0; i < N; ++i) v[i] = __bfloat162float(p[i]);
+    }
+  }
+  static __device__ __forceinline__ void store(__nv_bfloat16* p, const float (&v)[N]) {
+    if constexpr (N == 4) {
+      uint2 t = make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]));
+      *reinterpret_cast<uint2*>(p) = t;
+    } else if constexpr (N == 2) {
+      *reinterpret_cast<uint32_t*>(p) = pack_bf16x2(v[0], v[1]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < N; ++i) p[i] = __float2bfloat16_rn(v[i]);
+    }
+  }
+};
+
+// ============================================================== input
+// Input of the stem, one of:
+//  kInDense : x (B, 4, L) fp32 or bf16 (NCL), any values
+//  kInBases : bases (B, L) int8, base b in 0..3 -> one-hot column, other
+//             values -> all-zero column
+//  kInIsm   : mutant m of an ISM pass: sequence seq = m_base / per_seq ... the
+//             mutant's bases are its reference's with one substitution
+enum : int { kInDense = 0, kInBases = 1, kInIsm = 2 };
+
+struct StemInput {
+  const void* x;          // kInDense
+  int x_bf16;             // kInDense: element type
+  const int8_t* bases;    // kInBases / kInIsm: (n_ref, L)
+  long long mut0;         // kInIsm: global index of this pass's first mutant
+  int ism_start;          // kInIsm: first mutated position
+  int ism_width;          // kInIsm: number of mutated positions
+};
+
+// Value of input channel k (0..3) at position p (0 <= p < L) of batch row b.
+template <int kIn>
+__device__ __forceinline__ void stem_column(const StemInput& in, int L, int b, int p,
+                                            float (&col)[4]) {
+  if constexpr (kIn == kInDense) {
+    if (in.x_bf16) {
+      const __nv_bfloat16* x = static_cast<const __nv_bfloat16*>(in.x);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) col[k] = __bfloat162float(x[((long long)b * 4 + k) * L + p]);
+    } else {
+      const float* x = static_cast<const float*>(in.x);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) col[k] = x[((long long)b * 4 + k) * L + p];
+    }
+  } else {
+    int base;
+    if constexpr (kIn == kInBases) {
+      base = in.bases[(long long)b * L + p];
+    } else {
+      // mutant index -> (reference n, position offset w, alternative k)
+      const long long m = in.mut0 + b;
+      const long long per_seq = 3LL * in.ism_width;
+      const int n = static_cast<int>(m / per_seq);
+      const int rem = static_cast<int>(m - (long long)n * per_seq);
+      const int w = rem / 3, k = rem - 3 * (rem / 3);
+      const int mp = in.ism_start + w;
+      base = in.bases[(long long)n * L + p];
+      if (p == mp) base = ((in.bases[(long long)n * L + mp] & 3) + 1 + k) & 3;
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) col[k] = (base == k) ? 1.0f : 0.0f;
+  }
+}
+
+// ============================================================== stem
+// X0[b, l, c] = gelu_tanh(bias[c] + sum_{k<4, t<21} W[c, k, t] x[b, k, l + t - 10])
+// (upstream cherimoya.py:173-174, 373). One thread per channel, kStemL
+// consecutive positions; the input window is staged in shared memory.
+constexpr int kStemL = 32;
+
+template <typename act_t, int kIn>
+__global__ void __launch_bounds__(256) stem_kernel(StemInput in, const float* __restrict__ w,
+                                                   const float* __restrict__ bias, act_t* X,
+                                                   int L, int C, int CP) {
+  __shared__ float win[4][kStemL + kStemTaps - 1];
+  const int b = blockIdx.y;
+  const int l0 = blockIdx.x * kStemL;
+  const int c = threadIdx.x;
+  for (int i = threadIdx.x; i < kStemL + kStemTaps - 1; i += blockDim.x) {
+    const int p = l0 + i - kStemPad;
+    float col[4] = {0.f, 0.f, 0.f, 0.f};
+    if (p >= 0 && p < L) stem_column<kIn>(in, L, b, p, col);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) win[k][i] = col[k];
+  }
+  __syncthreads();
+  if (c >= CP) return;
+  float acc[kStemL];
+  const float b0 = (c < C) ? bias[c] : 0.f;
+#pragma unroll
+  for (int i = 0; i < kStemL; ++i) acc[i] = b0;
+  if (c < C) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+#pragma unroll
+      for (int t = 0; t < kStemTaps; ++t) {
+        const float wt = w[(c * 4 + k) * kStemTaps + t];
+#pragma unroll
+        for (int i = 0; i < kStemL; ++i) acc[i] = fmaf(wt, win[k][i + t], acc[i]);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kStemL; ++i) {
+    const int l = l0 + i;
+    if (l < L) {
+      const float v = acc[i];
+      const float y = (c < C) ? 0.5f * v * (1.0f + tanhf(0.7978845608028654f *
+                                                          (v + 0.044715f * v * v * v)))
+                              : 0.f;
+      X[((long long)b * L + l) * CP + c] = from_f32<act_t>(y);
+    }
+  }
+}
+
+// ============================================================== stats
+// Per-example LayerNorm statistics of the dilated depthwise conv output
+// y = w0 x[l-d] + w1 x[l] + w2 x[l+d] over the (L, C) plane (upstream
+// cheri.py:84-98). Each block reduces kStatsRows rows to (count, mean, M2)
+// with a two-pass in-register reduction; the last block of an example
+// combines the partials in index order (Chan et al.'s pairwise update), so
+// the result is deterministic. Writes stats[b] = (mean, 1/sqrt(var + eps)).
+template <typename act_t, int CP>
+__global__ void __launch_bounds__(256) stats_kernel(const act_t* __restrict__ X,
+                                                    const float* __restrict__ convw, int dil,
+                                                    int L, int C, float eps,
+                                                    float* __restrict__ partials,
+                                                    unsigned int* __restrict__ counters,
+                                                    float2* __restrict__ stats) {
+  constexpr int CPL = CP / 32;             // channels per lane
+  constexpr int kRowsPerWarp = kStatsRows / 8;
+  __shared__ float red[8];
+  __shared__ float s_mean;
+  __shared__ bool s_last;
+  const int b = blockIdx.y;
+  const int chunk = blockIdx.x;
+  const int n_chunks = gridDim.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c0 = lane * CPL;
+  float w0[CPL], w1[CPL], w2[CPL];
+#pragma unroll
+  for (int j = 0; j < CPL; ++j) {
+    w0[j] = convw[c0 + j];
+    w1[j] = convw[CP + c0 + j];
+    w2[j] = convw[2 * CP + c0 + j];
+  }
+  const act_t* Xb = X + (long long)b * L * CP;
+  float y[kRowsPerWarp][CPL];
+  float s = 0.f;
+  const int row_base = chunk * kStatsRows + warp * kRowsPerWarp;
+#pragma unroll
+  for (int i = 0; i < kRowsPerWarp; ++i) {
+    const int l = row_base + i;
+    float xc[CPL], xl[CPL], xr[CPL];
+#pragma unroll
+    for (int j = 0; j < CPL; ++j) { xc[j] = 0.f; xl[j] = 0.f; xr[j] = 0.f; }
+    if (l < L) {
+      Vec<act_t, CPL>::load(Xb + (long long)l * CP + c0, xc);
+      if (l - dil >= 0) Vec<act_t, CPL>::load(Xb + (long long)(l - dil) * CP + c0, xl);
+      if (l + dil < L) Vec<act_t, CPL>::load(Xb + (long long)(l + dil) * CP + c0, xr);
+    }
+#pragma unroll
+    for (int j = 0; j < CPL; ++j) {
+      const float v = fmaf(w0[j], xl[j], fmaf(w1[j], xc[j], w2[j] * xr[j]));
+      y[i][j] = (l < L && c0 + j < C) ? v : 0.f;
+      s += y[i][j];
+    }
+  }
+  const int rows_here = min(kStatsRows, L - chunk * kStatsRows);
+  const float count = static_cast<float>(rows_here) * static_cast<float>(C);
+  // pass 1: chunk mean
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) red[warp] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int i = 0; i < 8; ++i) t += red[i];
+    s_mean = t / count;
+  }
+  __syncthreads();
+  const float mean = s_mean;
+  // pass 2: sum of squared deviations from the chunk mean
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < kRowsPerWarp; ++i) {
+    const int l = row_base + i;
+#pragma unroll
+    for (int j = 0; j < CPL; ++j) {
+      const float dv = y[i][j] - mean;
+      q += (l < L && c0 + j < C) ? dv * dv : 0.f;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  __syncthreads();
+  if (lane == 0) red[warp] = q;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float m2 = 0.f;
+    for (int i = 0; i < 8; ++i) m2 += red[i];
+    float* part = partials + ((long long)b * n_chunks + chunk) * 3;
+    part[0] = count;
+    part[1] = mean;
+    part[2] = m2;
+    __threadfence();
+    const unsigned int prev = atomicAdd(&counters[b], 1u);
+    s_last = (prev == static_cast<unsigned int>(n_chunks - 1));
+  }
+  __syncthreads();
+  if (!s_last || threadIdx.x != 0) return;
+  __threadfence();
+  const volatile float* pb = partials + (long long)b * n_chunks * 3;
+  float na = pb[0], ma = pb[1], qa = pb[2];
+  for (int i = 1; i < n_chunks; ++i) {
+    const float nb = pb[i * 3], mb = pb[i * 3 + 1], qb = pb[i * 3 + 2];
+    const float nab = na + nb;
+    const float delta = mb - ma;
+    ma = ma + delta * (nb / nab);
+    qa = qa + qb + delta * delta * (na * nb / nab);
+    na = nab;
+  }
+  const float var = qa / na;
+  stats[b] = make_float2(ma, 1.0f / sqrtf(var + eps));
+  counters[b] = 0u;  // leave the counter ready for the next layer / call
+}
+
+// ============================================================== MLP
+// One Cheri Block update for 128-row tiles of the flattened (B*L) rows:
+//   A1 = bf16((conv(X) - mean) * rstd)            (built by all threads)
+//   D1 = A1 * W1^T                                (tcgen05, TMEM, fp32)
+//   A2 = bf16(gelu(D1))                           (TMEM -> registers -> smem)
+//   D2 = A2 * (rs * W2)^T                         (tcgen05, TMEM, fp32)
+//   X_out = X + D2
+// (upstream cheri.py:1072-1082; the Triton equivalent is
+// _fwd_inf_norm_mlp_kernel, cheri.py:594-669). Persistent: one CTA per SM,
+// W1/W2 resident in shared memory for the whole launch.
+struct MlpArgs {
+  const void* X_in;
+  void* X_out;
+  const float2* stats;
+  const uint8_t* w1;     // packed bf16 W1 tile (HP x CP, swizzled)
+  const uint8_t* w2;     // packed bf16 rs*W2 tile (CP x HP, swizzled)
+  const float* convw;    // (3, CP) fp32
+  int dil;
+  int L;
+  int C;
+  long long rows;        // B * L
+  int n_tiles;
+  int* status;
+};
+
+template <int CP, int HP>
+struct MlpSmem {
+  static constexpr uint32_t kW1 = 0;
+  static constexpr uint32_t kW2 = kW1 + HP * CP * 2;
+  static constexpr uint32_t kA2 = kW2 + CP * HP * 2;   // A1 aliases the start of A2
+  static constexpr uint32_t kBar = kA2 + kTileRows * HP * 2;
+  static constexpr uint32_t kSlot = kBar + 16;
+  static constexpr uint32_t kBytes = kSlot + 16;
+  static constexpr uint32_t kAlloc = kBytes + 1024;      // room to align the base to 1024
+};
+
+template <typename act_t, int CP, int HP, bool kFastGelu>
+__global__ void __launch_bounds__(128, 1) mlp_kernel(MlpArgs a) {
+  static_assert(CP % 64 == 0 && HP % 64 == 0 && HP >= CP && HP <= 256 && CP <= 128,
+                "tile shapes");
+  using S = MlpSmem<CP, HP>;
+  constexpr int CPL = CP / 32;
+  constexpr uint32_t kTmemCols = 512;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sW1 = smem + S::kW1;
+  uint8_t* sW2 = smem + S::kW2;
+  uint8_t* sA = smem + S::kA2;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kBar);
+  uint32_t* slot = reinterpret_cast<uint32_t*>(smem + S::kSlot);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const act_t* Xi = static_cast<const act_t*>(a.X_in);
+  act_t* Xo = static_cast<act_t*>(a.X_out);
+
+  if (warp == 0) tmem_alloc(slot, kTmemCols);
+  if (tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    mbar_init_fence();
+  }
+  {  // weights -> shared memory (already in the swizzled operand layout)
+    const uint4* g1 = reinterpret_cast<const uint4*>(a.w1);
+    const uint4* g2 = reinterpret_cast<const uint4*>(a.w2);
+    uint4* s1 = reinterpret_cast<uint4*>(sW1);
+    uint4* s2 = reinterpret_cast<uint4*>(sW2);
+    for (int i = tid; i < HP * CP * 2 / 16; i += blockDim.x) s1[i] = g1[i];
+    for (int i = tid; i < CP * HP * 2 / 16; i += blockDim.x) s2[i] = g2[i];
+  }
+  const int c0 = lane * CPL;
+  float cw0[CPL], cw1[CPL], cw2[CPL];
+#pragma unroll
+  for (int j = 0; j < CPL; ++j) {
+    cw0[j] = a.convw[c0 + j];
+    cw1[j] = a.convw[CP + c0 + j];
+    cw2[j] = a.convw[2 * CP + c0 + j];
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *slot;
+  const uint32_t tD1 = tmem;         // columns [0, HP)
+  const uint32_t tD2 = tmem + HP;    // columns [HP, HP + CP)
+  const uint32_t lane_sel = static_cast<uint32_t>(warp * 32) << 16;
+  const uint32_t sA_addr = smem_u32(sA), sW1_addr = smem_u32(sW1), sW2_addr = smem_u32(sW2);
+  constexpr uint32_t kIdesc1 = idesc_bf16(kTileRows, HP);
+  constexpr uint32_t kIdesc2 = idesc_bf16(kTileRows, CP);
+
+  bool failed = false;
+  uint32_t it = 0;
+  for (int tile = blockIdx.x; tile < a.n_tiles; tile += gridDim.x, ++it) {
+    const long long row0 = (long long)tile * kTileRows;
+    // ---- A1: conv + LayerNorm, bf16, swizzled (warp w builds rows 32w..32w+31)
+    for (int i = 0; i < 32; ++i) {
+      const int rl = warp * 32 + i;
+      const long long r = row0 + rl;
+      float v[CPL];
+#pragma unroll
+      for (int j = 0; j < CPL; ++j) v[j] = 0.f;
+      if (r < a.rows) {
+        const int n = static_cast<int>(r / a.L);
+        const int l = static_cast<int>(r - (long long)n * a.L);
+        const float2 st = a.stats[n];
+        float xc[CPL], xl[CPL], xr[CPL];
+#pragma unroll
+        for (int j = 0; j < CPL; ++j) { xl[j] = 0.f; xr[j] = 0.f; }
+        Vec<act_t, CPL>::load(Xi + r * CP + c0, xc);
+        if (l - a.dil >= 0) Vec<act_t, CPL>::load(Xi + (r - a.dil) * CP + c0, xl);
+        if (l + a.dil < a.L) Vec<act_t, CPL>::load(Xi + (r + a.dil) * CP + c0, xr);
+#pragma unroll
+        for (int j = 0; j < CPL; ++j) {
+          const float y = fmaf(cw0[j], xl[j], fmaf(cw1[j], xc[j], cw2[j] * xr[j]));
+          v[j] = (c0 + j < a.C) ? (y - st.x) * st.y : 0.f;
+        }
+      }
+      const uint32_t off = sw128_offset(rl, c0, kTileRows);
+      if constexpr (CPL == 4) {
+        *reinterpret_cast<uint2*>(sA + off) =
+            make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]));
+      } else {
+        *reinterpret_cast<uint32_t*>(sA + off) = pack_bf16x2(v[0], v[1]);
+      }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    // ---- GEMM1
+    if (tid == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int k = 0; k < CP / 16; ++k) {
+        const uint64_t da = desc_sw128(sA_addr + (k >> 2) * (kTileRows * 128) + (k & 3) * 32);
+        const uint64_t db = desc_sw128(sW1_addr + (k >> 2) * (HP * 128) + (k & 3) * 32);
+        mma_bf16(tD1, da, db, kIdesc1, k > 0 ? 1u : 0u);
+      }
+      mma_commit(&bars[0]);
+    }
+    bool ok = mbar_wait(&bars[0], it & 1);
+    if (__syncthreads_or(!ok)) { failed = true; break; }
+    tc_fence_after();
+    // ---- GELU: TMEM D1 -> bf16 A2 (thread = row 32*warp + lane)
+    {
+      const int rl = warp * 32 + lane;
+#pragma unroll 1
+      for (int j = 0; j < HP / 32; ++j) {
+        uint32_t r[32];
+        tmem_ld32(tD1 + lane_sel + j * 32, r);
+        tmem_ld_wait();
+        uint32_t p[16];
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          const float g0 = gelu_tanh<kFastGelu>(__uint_as_float(r[2 * q]));
+          const float g1 = gelu_tanh<kFastGelu>(__uint_as_float(r[2 * q + 1]));
+          p[q] = pack_bf16x2(g0, g1);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t off = sw128_offset(rl, j * 32 + q * 8, kTileRows);
+          *reinterpret_cast<uint4*>(sA + off) =
+              make_uint4(p[4 * q], p[4 * q + 1], p[4 * q + 2], p[4 * q + 3]);
+        }
+      }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    // ---- GEMM2
+    if (tid == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int k = 0; k < HP / 16; ++k) {
+        const uint64_t da = desc_sw128(sA_addr + (k >> 2) * (kTileRows * 128) + (k & 3) * 32);
+        const uint64_t db = desc_sw128(sW2_addr + (k >> 2) * (CP * 128) + (k & 3) * 32);
+        mma_bf16(tD2, da, db, kIdesc2, k > 0 ? 1u : 0u);
+      }
+      mma_commit(&bars[1]);
+    }
+    ok = mbar_wait(&bars[1], it & 1);
+    if (__syncthreads_or(!ok)) { failed = true; break; }
+    tc_fence_after();
+    // ---- residual: X_out = X_in + D2 (thread = row)
+    {
+      const long long r = row0 + warp * 32 + lane;
+#pragma unroll 1
+      for (int j = 0; j < CP / 32; ++j) {
+        uint32_t d[32];
+        tmem_ld32(tD2 + lane_sel + j * 32, d);
+        tmem_ld_wait();
+        if (r < a.rows) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            float x[4];
+            Vec<act_t, 4>::load(Xi + r * CP + j * 32 + q * 4, x);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) x[e] += __uint_as_float(d[q * 4 + e]);
+            Vec<act_t, 4>::store(Xo + r * CP + j * 32 + q * 4, x);
+          }
+        }
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+  }
+  if (failed && tid == 0) atomicExch(a.status, kStatusTimeout);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ============================================================== heads
+// Profile head: P[b, o, j] = bias[o] + sum_{c < Cin, t < 75} F[o, c, t]
+//   * Xc[b, c, T + j + t - 37],  j in [0, Lout)
+// where Xc = concat(X, X_ctl) along channels, zero outside [0, L)
+// (upstream cherimoya.py:182-184, 379-384). A block handles kHeadJ output
+// positions of one example; the input window is staged channel-major in
+// shared memory. Warp w sums channels c = w, w + 4, ...; lane i produces
+// kHeadPer consecutive positions with a sliding register window; the four
+// warp partials are added in a fixed order.
+constexpr int kHeadJ = 128;
+constexpr int kHeadPer = 4;
+constexpr int kHeadWarps = 4;
+constexpr int kHeadWin = kHeadJ + kHeadTaps - 1;   // 202
+
+template <typename act_t>
+__global__ void __launch_bounds__(kHeadWarps * 32) profile_head_kernel(
+    const act_t* __restrict__ X, const float* __restrict__ X_ctl, const float* __restrict__ F,
+    const float* __restrict__ fbias, float* __restrict__ profile, int L, int C, int CP,
+    int n_ctl, int n_out, int T, int Lout) {
+  extern __shared__ float win[];   // [Cin][kHeadWin], then [kHeadWarps][kHeadJ]
+  const int b = blockIdx.y;
+  const int j0 = blockIdx.x * kHeadJ;
+  const int Cin = C + n_ctl;
+  float* part = win + Cin * kHeadWin;
+  const int p0 = T + j0 - kHeadPad;     // sequence position of win[.][0]
+  for (int idx = threadIdx.x; idx < kHeadWin * Cin; idx += blockDim.x) {
+    const int w = idx / Cin, c = idx - (idx / Cin) * Cin;
+    const int p = p0 + w;
+    float v = 0.f;
+    if (p >= 0 && p < L) {
+      v = (c < C) ? to_f32<act_t>(X[((long long)b * L + p) * CP + c])
+                  : X_ctl[((long long)b * n_ctl + (c - C)) * L + p];
+    }
+    win[c * kHeadWin + w] = v;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int jl = lane * kHeadPer;
+  for (int o = 0; o < n_out; ++o) {
+    float acc[kHeadPer];
+#pragma unroll
+    for (int e = 0; e < kHeadPer; ++e) acc[e] = 0.f;
+    const float* Fo = F + (long long)o * Cin * kHeadTaps;
+    for (int c = warp; c < Cin; c += kHeadWarps) {
+      const float* wrow = win + c * kHeadWin + jl;
+      const float* frow = Fo + c * kHeadTaps;
+      float sw[kHeadPer];
+#pragma unroll
+      for (int e = 0; e < kHeadPer - 1; ++e) sw[e + 1] = wrow[e];
+#pragma unroll 5
+      for (int t = 0; t < kHeadTaps; ++t) {
+#pragma unroll
+        for (int e = 0; e < kHeadPer - 1; ++e) sw[e] = sw[e + 1];
+        sw[kHeadPer - 1] = wrow[t + kHeadPer - 1];
+        const float f = __ldg(frow + t);
+#pragma unroll
+        for (int e = 0; e < kHeadPer; ++e) acc[e] = fmaf(f, sw[e], acc[e]);
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < kHeadPer; ++e) part[warp * kHeadJ + jl + e] = acc[e];
+    __syncthreads();
+    if (warp == 0) {
+      const float bo = fbias[o];
+#pragma unroll
+      for (int e = 0; e < kHeadPer; ++e) {
+        const int j = j0 + jl + e;
+        float v = part[jl + e];
+#pragma unroll
+        for (int w = 1; w < kHeadWarps; ++w) v += part[w * kHeadJ + jl + e];
+        if (j < Lout) profile[((long long)b * n_out + o) * Lout + j] = v + bo;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// Count head: logcount[b, g] = bias[g] + sum_c Wl[g, c] mean_{l in [T, L-T)} X[b, l, c]
+//   (+ Wl[g, C] * log(1 + sum_{k, l in [T, L-T)} X_ctl[b, k, l]) with controls)
+// (upstream cherimoya.py:185-186, 387-399). One block per example, one
+// thread per channel.
+template <typename act_t>
+__global__ void __launch_bounds__(256) count_head_kernel(
+    const act_t* __restrict__ X, const float* __restrict__ X_ctl, const float* __restrict__ Wl,
+    const float* __restrict__ lbias, float* __restrict__ logcounts, int L, int C, int CP,
+    int n_ctl, int n_groups, int T) {
+  __shared__ float mean_s[256];
+  __shared__ float ctl_s;
+  __shared__ float red[8];
+  const int b = blockIdx.x;
+  const int c = threadIdx.x;
+  const int Lout = L - 2 * T;
+  if (c < C) {
+    float s = 0.f;
+    const act_t* Xb = X + ((long long)b * L + T) * CP + c;
+    for (int l = 0; l < Lout; ++l) s += to_f32<act_t>(Xb[(long long)l * CP]);
+    mean_s[c] = s / static_cast<float>(Lout);
+  }
+  if (threadIdx.x == 0) {
+    float cs = 0.f;
+    for (int k = 0; k < n_ctl; ++k) {
+      const float* xc = X_ctl + ((long long)b * n_ctl + k) * L + T;
+      for (int l = 0; l < Lout; ++l) cs += xc[l];
+    }
+    ctl_s = logf(cs + 1.0f);
+  }
+  __syncthreads();
+  const int Cin = C + (n_ctl > 0 ? 1 : 0);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int g = 0; g < n_groups; ++g) {
+    float v = 0.f;
+    if (c < C) v = Wl[(long long)g * Cin + c] * mean_s[c];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = lbias[g];
+      for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
+      if (n_ctl > 0) t += Wl[(long long)g * Cin + C] * ctl_s;
+      logcounts[(long long)b * n_groups + g] = t;
+    }
+    __syncthreads();
+  }
+}
+
+// ============================================================== scoring
+// Row-wise softmax of a reference profile flattened over (n_out, Lout).
+__global__ void __launch_bounds__(256) softmax_rows_kernel(const float* __restrict__ logits,
+                                                           float* __restrict__ probs, int len) {
+  __shared__ float red[8];
+  __shared__ float bcast;
+  const long long base = (long long)blockIdx.x * len;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float m = -INFINITY;
+  for (int i = threadIdx.x; i < len; i += blockDim.x) m = fmaxf(m, logits[base + i]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = red[0];
+    for (int i = 1; i < 8; ++i) t = fmaxf(t, red[i]);
+    bcast = t;
+  }
+  __syncthreads();
+  m = bcast;
+  float s = 0.f;
+  for (int i = threadIdx.x; i < len; i += blockDim.x) s += expf(logits[base + i] - m);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  __syncthreads();
+  if (lane == 0) red[warp] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int i = 0; i < 8; ++i) t += red[i];
+    bcast = t;
+  }
+  __syncthreads();
+  const float inv = 1.0f / bcast;
+  for (int i = threadIdx.x; i < len; i += blockDim.x)
+    probs[base + i] = expf(logits[base + i] - m) * inv;
+}
+
+// Jensen-Shannon distance between softmax(logits[i]) and probs[ref_of(i)]
+// over `len` values (upstream performance.py:138-207: zero-probability
+// terms contribute 0, natural log), plus the log-count delta of every
+// group. ref_of(i) = i / per_ref for ISM passes (i counted from mut0), or
+// i for variant pairs (per_ref = 1).
+__device__ __forceinline__ float kl_term(float p, float q) {
+  return (p != 0.f && q != 0.f) ? p * logf(p / q) : 0.f;
+}
+
+struct ScoreArgs {
+  const float* logits;      // (n, len) mutant / alt profiles
+  const float* ref_probs;   // (n_ref, len)
+  const float* lc;          // (n, n_groups) mutant / alt logcounts
+  const float* lc_ref;      // (n_ref, n_groups)
+  int len;
+  int n_groups;
+  long long mut0;           // global index of row 0 (ISM)
+  int per_ref;              // rows per reference (ISM: 3 * width; variants: 1)
+  int ism;                  // 1: ISM output layout, 0: variant layout
+  int ism_start, ism_width; // ISM: window
+  const int8_t* bases;      // ISM: reference bases (n_ref, L)
+  int L;
+  float* d_logcount;        // ISM: (n_ref, n_groups, 4, W); variant: (n, n_groups)
+  float* jsd;               // ISM: (n_ref, 4, W); variant: (n)
+};
+
+__global__ void __launch_bounds__(256) score_kernel(ScoreArgs a) {
+  __shared__ float red[8];
+  __shared__ float bcast;
+  const int row = blockIdx.x;
+  const long long gm = a.mut0 + row;
+  const int ref = static_cast<int>(gm / a.per_ref);
+  const float* x = a.logits + (long long)row * a.len;
+  const float* q = a.ref_probs + (long long)ref * a.len;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float m = -INFINITY;
+  for (int i = threadIdx.x; i < a.len; i += blockDim.x) m = fmaxf(m, x[i]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = red[0];
+    for (int i = 1; i < 8; ++i) t = fmaxf(t, red[i]);
+    bcast = t;
+  }
+  __syncthreads();
+  m = bcast;
+  float s = 0.f;
+  for (int i = threadIdx.x; i < a.len; i += blockDim.x) s += expf(x[i] - m);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  __syncthreads();
+  if (lane == 0) red[warp] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int i = 0; i < 8; ++i) t += red[i];
+    bcast = t;
+  }
+  __syncthreads();
+  const float inv = 1.0f / bcast;
+  float j = 0.f;
+  for (int i = threadIdx.x; i < a.len; i += blockDim.x) {
+    const float p1 = expf(x[i] - m) * inv;
+    const float p2 = q[i];
+    const float mid = 0.5f * (p1 + p2);
+    j += kl_term(p1, mid) + kl_term(p2, mid);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) j += __shfl_xor_sync(0xffffffffu, j, o);
+  __syncthreads();
+  if (lane == 0) red[warp] = j;
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  float jt = 0.f;
+  for (int i = 0; i < 8; ++i) jt += red[i];
+  jt *= 0.5f;
+  if (a.ism) {
+    const int rem = static_cast<int>(gm - (long long)ref * a.per_ref);
+    const int w = rem / 3, k = rem - 3 * (rem / 3);
+    const int p = a.ism_start + w;
+    const int alt = ((a.bases[(long long)ref * a.L + p] & 3) + 1 + k) & 3;
+    a.jsd[((long long)ref * 4 + alt) * a.ism_width + w] = jt;
+    for (int g = 0; g < a.n_groups; ++g) {
+      const float d = a.lc[(long long)row * a.n_groups + g] - a.lc_ref[(long long)ref * a.n_groups + g];
+      a.d_logcount[(((long long)ref * a.n_groups + g) * 4 + alt) * a.ism_width + w] = d;
+    }
+  } else {
+    a.jsd[gm] = jt;
+    for (int g = 0; g < a.n_groups; ++g)
+      a.d_logcount[gm * a.n_groups + g] =
+          a.lc[(long long)row * a.n_groups + g] - a.lc_ref[(long long)ref * a.n_groups + g];
+  }
+}
+
+// ISM entries whose base equals the reference base: the mutant is the
+// reference, both scores are 0.
+__global__ void ism_fill_ref_kernel(const int8_t* __restrict__ bases, int L, int start, int W,
+                                    int n_groups, int n_ref, float* d_logcount, float* jsd) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)n_ref * W) return;
+  const int n = static_cast<int>(i / W), w = static_cast<int>(i - (long long)n * W);
+  const int b = bases[(long long)n * L + start + w] & 3;
+  jsd[((long long)n * 4 + b) * W + w] = 0.f;
+  for (int g = 0; g < n_groups; ++g)
+    d_logcount[(((long long)n * n_groups + g) * 4 + b) * W + w] = 0.f;
+}
+
+// ============================================================== packing
+// fp32 (R, K) row-major source -> bf16 K-major 128B-swizzled tile of RP x KP
+// (zero padded), values multiplied by `scale`.
+__global__ void pack_sw128_kernel(const float* __restrict__ src, int R, int K, int RP, int KP,
+                                  float scale, uint8_t* __restrict__ dst) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= RP * KP) return;
+  const int r = i / KP, k = i - (i / KP) * KP;
+  const float v = (r < R && k < K) ? src[(long long)r * K + k] * scale : 0.f;
+  *reinterpret_cast<__nv_bfloat16*>(dst + sw128_offset(r, k, RP)) = __float2bfloat16_rn(v);
+}
+
+// fp32 (3, C) -> (3, CP) zero padded.
+__global__ void pack_convw_kernel(const float* __restrict__ src, int C, int CP,
+                                  float* __restrict__ dst) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= 3 * CP) return;
+  const int t = i / CP, c = i - (i / CP) * CP;
+  dst[i] = (c < C) ? src[t * C + c] : 0.f;
+}
+
+// (rows, C) <-> (rows, CP) channel padding of activations.
+template <typename act_t>
+__global__ void pad_channels_kernel(const act_t* __restrict__ src, act_t* __restrict__ dst,
+                                    long long rows, int C, int CP) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * CP) return;
+  const long long r = i / CP;
+  const int c = static_cast<int>(i - r * CP);
+  dst[i] = (c < C) ? src[r * C + c] : from_f32<act_t>(0.f);
+}
+template <typename act_t>
+__global__ void unpad_channels_kernel(const act_t* __restrict__ src, act_t* __restrict__ dst,
+                                      long long rows, int C, int CP) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * C) return;
+  const long long r = i / C;
+  const int c = static_cast<int>(i - r * C);
+  dst[i] = src[r * CP + c];
+}
+
+__global__ void copy_f32_kernel(const float* __restrict__ src, float* __restrict__ dst, long long n) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) dst[i] = src[i];
+}
+
+}  // namespace chm
