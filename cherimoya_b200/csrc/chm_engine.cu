@@ -177,6 +177,20 @@ int launch_mlp_t(const MlpArgs& a, int grid, cudaStream_t st, bool fast) {
 template <typename act_t>
 int launch_mlp(const Dims& m, const MlpArgs& a, int grid, cudaStream_t st) {
   const bool fast = (m.mode == CHM_MODE_BF16);
+  if (m.CP == ws::kC && m.HP == ws::kH) {
+    const int smem = ws::kAlloc;
+    LaunchTimer timer(kKMlp, st);
+    if (fast) {
+      auto k = mlp_ws_kernel<act_t, true>;
+      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      k<<<grid, ws::kThreads, smem, st>>>(a);
+    } else {
+      auto k = mlp_ws_kernel<act_t, false>;
+      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      k<<<grid, ws::kThreads, smem, st>>>(a);
+    }
+    return launch_status();
+  }
   if (m.CP == 64) {
     switch (m.HP) {
       case 64: return launch_mlp_t<act_t, 64, 64>(a, grid, st, fast);
@@ -197,14 +211,15 @@ int launch_mlp(const Dims& m, const MlpArgs& a, int grid, cudaStream_t st) {
 template <typename act_t>
 int launch_stats(const Dims& m, const act_t* X, const float* convw, int dil, int batch,
                  float* partials, unsigned* counters, float2* stats, cudaStream_t st) {
-  dim3 grid(m.n_chunks(), batch);
+  (void)partials;
+  (void)counters;
   LaunchTimer timer(kKStats, st);
   if (m.CP == 64) {
-    stats_kernel<act_t, 64><<<grid, 256, 0, st>>>(X, convw, dil, m.L, m.C, 1e-3f, partials,
-                                                  counters, stats);
+    stats_example_kernel<act_t, 64><<<batch, kStats2Threads, 0, st>>>(X, convw, dil, m.L, m.C,
+                                                                      1e-3f, stats);
   } else if (m.CP == 128) {
-    stats_kernel<act_t, 128><<<grid, 256, 0, st>>>(X, convw, dil, m.L, m.C, 1e-3f, partials,
-                                                   counters, stats);
+    stats_example_kernel<act_t, 128><<<batch, kStats2Threads, 0, st>>>(X, convw, dil, m.L, m.C,
+                                                                       1e-3f, stats);
   } else {
     return CHM_ERR_UNSUPPORTED;
   }

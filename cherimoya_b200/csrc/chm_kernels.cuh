@@ -7,6 +7,7 @@
 #pragma once
 #include <cuda_bf16.h>
 #include <cstdint>
+#include <type_traits>
 
 #include "chm_ptx.cuh"
 
@@ -88,6 +89,72 @@ template <int N> struct Vec<__nv_bfloat16, N> {
     }
   }
 };
+
+__device__ __forceinline__ void unpack4(const uint2& t, float (&v)[4]) {
+  v[0] = __uint_as_float(t.x << 16);
+  v[1] = __uint_as_float(t.x & 0xFFFF0000u);
+  v[2] = __uint_as_float(t.y << 16);
+  v[3] = __uint_as_float(t.y & 0xFFFF0000u);
+}
+__device__ __forceinline__ void unpack4(const float4& t, float (&v)[4]) {
+  v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+}
+
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&v)[8]) {
+  const uint4 t = *reinterpret_cast<const uint4*>(p);
+  v[0] = __uint_as_float(t.x << 16); v[1] = __uint_as_float(t.x & 0xFFFF0000u);
+  v[2] = __uint_as_float(t.y << 16); v[3] = __uint_as_float(t.y & 0xFFFF0000u);
+  v[4] = __uint_as_float(t.z << 16); v[5] = __uint_as_float(t.z & 0xFFFF0000u);
+  v[6] = __uint_as_float(t.w << 16); v[7] = __uint_as_float(t.w & 0xFFFF0000u);
+}
+__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  const float4 b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+struct Raw8f {
+  float4 a, b;
+};
+template <typename R, typename T>
+__device__ __forceinline__ R ldraw(const T* p) {
+  if constexpr (sizeof(R) == 16) {
+    return *reinterpret_cast<const R*>(p);
+  } else {
+    R r;
+    r.a = *reinterpret_cast<const float4*>(p);
+    r.b = *reinterpret_cast<const float4*>(p + 4);
+    return r;
+  }
+}
+__device__ __forceinline__ void unpack8(const uint4& t, float (&v)[8]) {
+  v[0] = __uint_as_float(t.x << 16); v[1] = __uint_as_float(t.x & 0xFFFF0000u);
+  v[2] = __uint_as_float(t.y << 16); v[3] = __uint_as_float(t.y & 0xFFFF0000u);
+  v[4] = __uint_as_float(t.z << 16); v[5] = __uint_as_float(t.z & 0xFFFF0000u);
+  v[6] = __uint_as_float(t.w << 16); v[7] = __uint_as_float(t.w & 0xFFFF0000u);
+}
+__device__ __forceinline__ void unpack8(const Raw8f& t, float (&v)[8]) {
+  v[0] = t.a.x; v[1] = t.a.y; v[2] = t.a.z; v[3] = t.a.w;
+  v[4] = t.b.x; v[5] = t.b.y; v[6] = t.b.z; v[7] = t.b.w;
+}
+
+// 16 bytes of activations plus the matching fp32 MLP outputs (raw bits).
+template <typename act_t>
+__device__ __forceinline__ uint4 add_residual(const uint4& x, const uint32_t* d) {
+  if constexpr (sizeof(act_t) == 2) {
+    float v[8];
+    unpack8(x, v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] += __uint_as_float(d[e]);
+    return make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                      pack_bf16x2(v[6], v[7]));
+  } else {
+    return make_uint4(__float_as_uint(__uint_as_float(x.x) + __uint_as_float(d[0])),
+                      __float_as_uint(__uint_as_float(x.y) + __uint_as_float(d[1])),
+                      __float_as_uint(__uint_as_float(x.z) + __uint_as_float(d[2])),
+                      __float_as_uint(__uint_as_float(x.w) + __uint_as_float(d[3])));
+  }
+}
 
 // ============================================================== input
 // Input of the stem, one of:
@@ -304,6 +371,94 @@ __global__ void __launch_bounds__(256) stats_kernel(const act_t* __restrict__ X,
   counters[b] = 0u;  // leave the counter ready for the next layer / call
 }
 
+// Per-example statistics, one block per example (replaces the chunked
+// version for the bandwidth-bound hot path). Lanes read 8 channels (16 B
+// bf16 / 32 B fp32); CP/8 lanes cover one row, so a warp streams 256/CP*...
+// rows per load instruction. Each thread accumulates sum(y) and sum(y^2)
+// of one row's 8 channels in fp32 and adds them into fp64 accumulators; the
+// block reduction is fp64 in a fixed order, so the result is deterministic
+// and var = E[y^2] - mean^2 does not cancel catastrophically.
+constexpr int kStats2Threads = 512;
+
+template <typename act_t, int CP>
+__global__ void __launch_bounds__(kStats2Threads) stats_example_kernel(
+    const act_t* __restrict__ X, const float* __restrict__ convw, int dil, int L, int C,
+    float eps, float2* __restrict__ stats) {
+  constexpr int kLanesPerRow = CP / 8;
+  constexpr int kRowsPerPass = kStats2Threads / kLanesPerRow;
+  // 8 channels: one uint4 of bf16, or two float4 of fp32
+  using raw_t = typename std::conditional<sizeof(act_t) == 2, uint4, Raw8f>::type;
+  __shared__ double red_s[kStats2Threads / 32], red_q[kStats2Threads / 32];
+  const int b = blockIdx.x;
+  const int sub = threadIdx.x % kLanesPerRow;
+  const int rsub = threadIdx.x / kLanesPerRow;
+  const int c0 = sub * 8;
+  float w0[8], w1[8], w2[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    w0[j] = convw[c0 + j];
+    w1[j] = convw[CP + c0 + j];
+    w2[j] = convw[2 * CP + c0 + j];
+    if (c0 + j >= C) { w0[j] = 0.f; w1[j] = 0.f; w2[j] = 0.f; }
+  }
+  const act_t* Xb = X + (long long)b * L * CP + c0;
+  double S = 0.0, Q = 0.0;
+  constexpr int kU = sizeof(act_t) == 2 ? 4 : 2;   // rows in flight per thread
+  for (int l0 = rsub; l0 < L; l0 += kRowsPerPass * kU) {
+    raw_t xc[kU], xl[kU], xr[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int l = l0 + u * kRowsPerPass;
+      xc[u] = raw_t{}; xl[u] = raw_t{}; xr[u] = raw_t{};
+      if (l < L) {
+        xc[u] = ldraw<raw_t>(Xb + (long long)l * CP);
+        if (l - dil >= 0) xl[u] = ldraw<raw_t>(Xb + (long long)(l - dil) * CP);
+        if (l + dil < L) xr[u] = ldraw<raw_t>(Xb + (long long)(l + dil) * CP);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      float fc[8], fl[8], fr[8];
+      unpack8(xc[u], fc);
+      unpack8(xl[u], fl);
+      unpack8(xr[u], fr);
+      float s = 0.f, q = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float y = fmaf(w0[j], fl[j], fmaf(w1[j], fc[j], w2[j] * fr[j]));
+        s += y;
+        q = fmaf(y, y, q);
+      }
+      S += static_cast<double>(s);
+      Q += static_cast<double>(q);
+    }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    S += __shfl_xor_sync(0xffffffffu, S, o);
+    Q += __shfl_xor_sync(0xffffffffu, Q, o);
+  }
+  if (lane == 0) {
+    red_s[warp] = S;
+    red_q[warp] = Q;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double s = 0.0, q = 0.0;
+    for (int i = 0; i < kStats2Threads / 32; ++i) {
+      s += red_s[i];
+      q += red_q[i];
+    }
+    const double n = static_cast<double>(L) * static_cast<double>(C);
+    const double mean = s / n;
+    double var = q / n - mean * mean;
+    if (var < 0.0) var = 0.0;
+    stats[b] = make_float2(static_cast<float>(mean),
+                           static_cast<float>(1.0 / sqrt(var + static_cast<double>(eps))));
+  }
+}
+
 // ============================================================== MLP
 // One Cheri Block update for 128-row tiles of the flattened (B*L) rows:
 //   A1 = bf16((conv(X) - mean) * rstd)            (built by all threads)
@@ -515,6 +670,303 @@ __global__ void __launch_bounds__(128, 1) mlp_kernel(MlpArgs a) {
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ============================================================== MLP, pipelined
+// Warp-specialised persistent version of mlp_kernel for the default width
+// (C = 128, H = 256). Roles, per CTA (one CTA per SM):
+//   warps 0-3  producer : conv + LayerNorm of tile t -> A1 (bf16, swizzled)
+//   warps 4-11 epilogue : GELU of D1 halves -> A2a / A2b, residual of D2
+//   warp 12    MMA      : one elected thread issues all tcgen05.mma
+// H is split in halves (a: h 0..127, b: h 128..255) so the GELU of one half
+// overlaps the MMAs of the other. The tensor pipe runs, per tile t,
+//   G2a(t)  G1a(t+1)  G2b(t)  G1b(t+1)
+// with G1x: D1x = A1 * W1[x]^T and G2x: D2 (+)= A2x * W2[:, x]^T.
+// TMEM (512 columns): D1a | D1b | D2[0] | D2[1] (D2 double-buffered so the
+// residual of tile t overlaps the MMAs of tile t+1).
+// Shared memory: W1 64 KB + W2 64 KB (resident), A1 32 KB, A2a + A2b 64 KB.
+namespace ws {
+constexpr int kC = 128, kH = 256, kHalf = 128;
+constexpr int kProducerWarps = 4, kEpilogueWarps = 8;
+constexpr int kMmaWarp = kProducerWarps + kEpilogueWarps;      // 12
+constexpr int kThreads = (kMmaWarp + 1) * 32;                   // 416
+constexpr uint32_t kW1 = 0;                                     // 256 x 128 bf16
+constexpr uint32_t kW2 = kW1 + kH * kC * 2;                     // 128 x 256 bf16
+constexpr uint32_t kA1 = kW2 + kC * kH * 2;                     // 128 x 128
+constexpr uint32_t kA2a = kA1 + kTileRows * kC * 2;             // 128 x 128
+constexpr uint32_t kA2b = kA2a + kTileRows * kHalf * 2;         // 128 x 128
+constexpr uint32_t kBars = kA2b + kTileRows * kHalf * 2;
+enum Bar { A1_FULL, A1_EMPTY, D1A_FULL, D1B_FULL, A2A_FULL, A2B_FULL, A2A_EMPTY, A2B_EMPTY,
+           D2_FULL0, D2_FULL1, D2_EMPTY0, D2_EMPTY1, kNumBars };
+constexpr uint32_t kSlot = kBars + kNumBars * 8;
+constexpr uint32_t kAbort = kSlot + 4;
+constexpr uint32_t kBytes = kAbort + 4;
+constexpr uint32_t kAlloc = kBytes + 1024;
+}  // namespace ws
+
+template <typename act_t, bool kFastGelu>
+__global__ void __launch_bounds__(ws::kThreads, 1) mlp_ws_kernel(MlpArgs a) {
+  using namespace ws;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBars);
+  uint32_t* slot = reinterpret_cast<uint32_t*>(smem + kSlot);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kAbort);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const act_t* Xi = static_cast<const act_t*>(a.X_in);
+  act_t* Xo = static_cast<act_t*>(a.X_out);
+
+  if (warp == kMmaWarp) tmem_alloc(slot, 512);
+  if (tid == 0) {
+    const uint32_t counts[kNumBars] = {kProducerWarps * 32, 1, 1, 1, kEpilogueWarps * 32,
+                                       kEpilogueWarps * 32, 1, 1, 1, 1, kEpilogueWarps * 32,
+                                       kEpilogueWarps * 32};
+    for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], counts[i]);
+    *abort_flag = 0;
+    mbar_init_fence();
+  }
+  {
+    const uint4* g1 = reinterpret_cast<const uint4*>(a.w1);
+    const uint4* g2 = reinterpret_cast<const uint4*>(a.w2);
+    uint4* s1 = reinterpret_cast<uint4*>(smem + kW1);
+    uint4* s2 = reinterpret_cast<uint4*>(smem + kW2);
+    for (int i = tid; i < kH * kC * 2 / 16; i += blockDim.x) s1[i] = g1[i];
+    for (int i = tid; i < kC * kH * 2 / 16; i += blockDim.x) s2[i] = g2[i];
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *slot;
+  const int first = blockIdx.x;
+  const int stride = gridDim.x;
+  const int n_my = (a.n_tiles > first) ? (a.n_tiles - first + stride - 1) / stride : 0;
+
+  if (warp < kProducerWarps) {
+    // ------------------------------------------------------------ producer
+    // lane pair (i, i+16) covers two rows; each lane 8 channels (16 B bf16)
+    constexpr int CPL = 8;
+    const int rsel = lane >> 4;
+    const int c0 = (lane & 15) * CPL;
+    float cw0[CPL], cw1[CPL], cw2[CPL];
+#pragma unroll
+    for (int j = 0; j < CPL; ++j) {
+      const bool live = c0 + j < a.C;
+      cw0[j] = live ? a.convw[c0 + j] : 0.f;
+      cw1[j] = live ? a.convw[kC + c0 + j] : 0.f;
+      cw2[j] = live ? a.convw[2 * kC + c0 + j] : 0.f;
+    }
+    using raw_t = typename std::conditional<sizeof(act_t) == 2, uint4, Raw8f>::type;
+    constexpr int kU = sizeof(act_t) == 2 ? 4 : 2;  // row pairs in flight per thread
+    uint8_t* sA1 = smem + kA1;
+    for (int it = 0; it < n_my; ++it) {
+      const long long row0 = (long long)(first + it * stride) * kTileRows;
+      bool waited = false;
+      for (int p0 = 0; p0 < 16; p0 += kU) {
+        raw_t xc[kU], xl[kU], xr[kU];
+        float2 st[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const long long r = row0 + warp * 32 + (p0 + u) * 2 + rsel;
+          xc[u] = raw_t{}; xl[u] = raw_t{}; xr[u] = raw_t{};
+          st[u] = make_float2(0.f, 0.f);
+          if (r < a.rows) {
+            const int n = static_cast<int>(r / a.L);
+            const int l = static_cast<int>(r - (long long)n * a.L);
+            st[u] = a.stats[n];
+            xc[u] = ldraw<raw_t>(Xi + r * kC + c0);
+            if (l - a.dil >= 0) xl[u] = ldraw<raw_t>(Xi + (r - a.dil) * kC + c0);
+            if (l + a.dil < a.L) xr[u] = ldraw<raw_t>(Xi + (r + a.dil) * kC + c0);
+          }
+        }
+        // the first batch of loads is in flight before waiting for the buffer
+        if (!waited) {
+          if (!mbar_wait_abortable(&bars[A1_EMPTY], (it & 1) ^ 1, abort_flag)) break;
+          waited = true;
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          float fc[CPL], fl[CPL], fr[CPL];
+          unpack8(xc[u], fc);
+          unpack8(xl[u], fl);
+          unpack8(xr[u], fr);
+          float v[CPL];
+          const float shift = -st[u].x * st[u].y;
+#pragma unroll
+          for (int j = 0; j < CPL; ++j) {
+            const float y = fmaf(cw0[j], fl[j], fmaf(cw1[j], fc[j], cw2[j] * fr[j]));
+            v[j] = fmaf(y, st[u].y, shift);
+          }
+          const int rl = warp * 32 + (p0 + u) * 2 + rsel;
+          *reinterpret_cast<uint4*>(sA1 + sw128_offset(rl, c0, kTileRows)) =
+              make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
+                         pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+        }
+      }
+      if (!waited) break;
+      fence_async_smem();
+      mbar_arrive(&bars[A1_FULL]);
+    }
+  } else if (warp < kMmaWarp) {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp - kProducerWarps;          // 0..7
+    const int quarter = warp & 3;                  // TMEM lane quarter of this warp
+    const int colhalf = ew >> 2;                   // 0: columns 0-63, 1: 64-127
+    const int rl = quarter * 32 + lane;            // tile row of this thread
+    const uint32_t lane_sel = static_cast<uint32_t>(quarter * 32) << 16;
+    for (int it = 0; it < n_my; ++it) {
+      const long long row0 = (long long)(first + it * stride) * kTileRows;
+      bool ok = true;
+#pragma unroll 1
+      for (int hh = 0; hh < 2 && ok; ++hh) {
+        // GELU of half hh: D1x -> A2x
+        ok = mbar_wait_abortable(&bars[hh ? D1B_FULL : D1A_FULL], it & 1, abort_flag) &&
+             mbar_wait_abortable(&bars[hh ? A2B_EMPTY : A2A_EMPTY], (it & 1) ^ 1, abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        uint8_t* sA2 = smem + (hh ? kA2b : kA2a);
+        const uint32_t tcol = tmem + hh * kHalf + colhalf * 64;
+#pragma unroll 1
+        for (int j = 0; j < 2; ++j) {
+          uint32_t r[32];
+          tmem_ld32(tcol + lane_sel + j * 32, r);
+          tmem_ld_wait();
+          uint32_t p[16];
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            if constexpr (kFastGelu) {
+              p[q] = gelu_bf16x2(__uint_as_float(r[2 * q]), __uint_as_float(r[2 * q + 1]));
+            } else {
+              p[q] = pack_bf16x2(gelu_tanh<false>(__uint_as_float(r[2 * q])),
+                                 gelu_tanh<false>(__uint_as_float(r[2 * q + 1])));
+            }
+          }
+          const int kbase = colhalf * 64 + j * 32;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            *reinterpret_cast<uint4*>(sA2 + sw128_offset(rl, kbase + q * 8, kTileRows)) =
+                make_uint4(p[4 * q], p[4 * q + 1], p[4 * q + 2], p[4 * q + 3]);
+          }
+        }
+        fence_async_smem();
+        tc_fence_before();
+        mbar_arrive(&bars[hh ? A2B_FULL : A2A_FULL]);
+      }
+      if (!ok) break;
+      // residual of D2[b]; the thread's input channels are fetched before the
+      // wait (they do not depend on the MMAs)
+      const int b = it & 1;
+      const long long r = row0 + rl;
+      const bool rv = r < a.rows;
+      constexpr int kVE = 16 / sizeof(act_t);      // elements per 16-byte vector
+      constexpr int kPre = 32 / kVE;                // vectors of one 32-column chunk
+      const act_t* xrow = Xi + r * kC + colhalf * 64;
+      act_t* orow = Xo + r * kC + colhalf * 64;
+      uint4 xin[kPre];
+#pragma unroll
+      for (int q = 0; q < kPre; ++q) xin[q] = rv ? *reinterpret_cast<const uint4*>(xrow + q * kVE)
+                                              : make_uint4(0, 0, 0, 0);
+      if (!mbar_wait_abortable(&bars[D2_FULL0 + b], (it >> 1) & 1, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t tcol = tmem + 2 * kHalf + b * kC + colhalf * 64;
+#pragma unroll 1
+      for (int j = 0; j < 2; ++j) {
+        uint32_t d[32];
+        tmem_ld32(tcol + lane_sel + j * 32, d);
+        if (j == 1) {
+#pragma unroll
+          for (int q = 0; q < kPre; ++q)
+            xin[q] = rv ? *reinterpret_cast<const uint4*>(xrow + 32 + q * kVE)
+                        : make_uint4(0, 0, 0, 0);
+        }
+        tmem_ld_wait();
+        if (rv) {
+#pragma unroll
+          for (int q = 0; q < kPre; ++q)
+            *reinterpret_cast<uint4*>(orow + j * 32 + q * kVE) =
+                add_residual<act_t>(xin[q], d + q * kVE);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bars[D2_EMPTY0 + b]);
+    }
+  } else {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && n_my > 0) {
+      const uint32_t sA1 = smem_u32(smem + kA1), sW1 = smem_u32(smem + kW1);
+      const uint32_t sW2 = smem_u32(smem + kW2);
+      const uint32_t sA2[2] = {smem_u32(smem + kA2a), smem_u32(smem + kA2b)};
+      constexpr uint32_t kIdesc = idesc_bf16(kTileRows, 128);
+      auto g1 = [&](int hh) {  // D1x = A1 * W1[hh*128 : hh*128+128]^T, K = 128
+        const uint32_t d = tmem + hh * kHalf;
+#pragma unroll
+        for (int k = 0; k < kC / 16; ++k) {
+          const uint64_t da = desc_sw128(sA1 + (k >> 2) * (kTileRows * 128) + (k & 3) * 32);
+          const uint64_t db =
+              desc_sw128(sW1 + (k >> 2) * (kH * 128) + hh * (kHalf * 128) + (k & 3) * 32);
+          mma_bf16(d, da, db, kIdesc, k > 0 ? 1u : 0u);
+        }
+      };
+      auto g2 = [&](int hh, int b) {  // D2[b] (+)= A2x * W2[:, x]^T, K = 128
+        const uint32_t d = tmem + 2 * kHalf + b * kC;
+#pragma unroll
+        for (int k = 0; k < kHalf / 16; ++k) {
+          const uint64_t da = desc_sw128(sA2[hh] + (k >> 2) * (kTileRows * 128) + (k & 3) * 32);
+          const uint64_t db =
+              desc_sw128(sW2 + (hh * 2 + (k >> 2)) * (kC * 128) + (k & 3) * 32);
+          mma_bf16(d, da, db, kIdesc, (hh > 0 || k > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait_abortable(&bars[A1_FULL], 0, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        g1(0);
+        mma_commit(&bars[D1A_FULL]);
+        g1(1);
+        mma_commit(&bars[D1B_FULL]);
+        mma_commit(&bars[A1_EMPTY]);
+      }
+      for (int it = 0; ok && it < n_my; ++it) {
+        const int b = it & 1;
+        const bool next = it + 1 < n_my;
+        ok = mbar_wait_abortable(&bars[A2A_FULL], it & 1, abort_flag) &&
+             mbar_wait_abortable(&bars[D2_EMPTY0 + b], ((it >> 1) & 1) ^ 1, abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        g2(0, b);
+        mma_commit(&bars[A2A_EMPTY]);
+        if (next) {
+          ok = mbar_wait_abortable(&bars[A1_FULL], (it + 1) & 1, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          g1(0);
+          mma_commit(&bars[D1A_FULL]);
+        }
+        ok = mbar_wait_abortable(&bars[A2B_FULL], it & 1, abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        g2(1, b);
+        mma_commit(&bars[A2B_EMPTY]);
+        mma_commit(&bars[D2_FULL0 + b]);
+        if (next) {
+          g1(1);
+          mma_commit(&bars[D1B_FULL]);
+          mma_commit(&bars[A1_EMPTY]);
+        }
+      }
+    }
+    __syncwarp();
+  }
+  // drain: every MMA this CTA issued has been waited on by the epilogue
+  // (D2_FULL of the last tile) unless the pipeline aborted.
+  tc_fence_before();
+  __syncthreads();
+  if (tid == 0 && *abort_flag) atomicExch(a.status, kStatusTimeout);
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
   }
 }
 

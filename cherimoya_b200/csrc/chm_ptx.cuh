@@ -26,22 +26,58 @@ __device__ __forceinline__ void mbar_init_fence() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
+__device__ __forceinline__ bool mbar_try(uint32_t addr, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
 // Returns true when the phase with the given parity has completed, false if
 // the bounded wait gave up.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   const uint32_t addr = smem_u32(bar);
   for (long long it = 0; it < kWaitLimit; ++it) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(addr), "r"(parity)
-        : "memory");
-    if (done) return true;
+    if (mbar_try(addr, parity)) return true;
   }
   return false;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wait bounded by wall time (kWaitNs) and by a block-wide abort flag that a
+// thread whose own wait gave up sets: a stuck pipeline drains in about
+// kWaitNs instead of each dependent wait running out in turn.
+constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s
+__device__ __forceinline__ bool mbar_wait_abortable(uint64_t* bar, uint32_t parity,
+                                                    volatile int* abort_flag) {
+  const uint32_t addr = smem_u32(bar);
+  if (mbar_try(addr, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try(addr, parity)) return true;
+    if ((it & 255u) == 0) {
+      if (*abort_flag) return false;
+      if (global_ns() - t0 > kWaitNs) {
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar))
+               : "memory");
 }
 
 // ---------------------------------------------------------------- fences
@@ -170,6 +206,25 @@ __device__ __forceinline__ float gelu_tanh(float x) {
   } else {
     return __fdividef(x, 1.0f + __expf(-2.0f * u));
   }
+}
+
+// GELU(tanh) of two values in packed bf16x2 arithmetic (bf16 mode): the
+// result is rounded to bf16 anyway, so u, tanh(u) and the final
+// 0.5 x (1 + tanh u) are evaluated with bf16x2 FMAs and tanh.approx.bf16x2,
+// three issue slots per value.
+__device__ __forceinline__ uint32_t gelu_bf16x2(float z0, float z1) {
+  uint32_t x, sq, t, u, th, hx, g;
+  asm("cvt.rn.bf16x2.f32 %0, %2, %1;" : "=r"(x) : "f"(z0), "f"(z1));
+  const uint32_t k1 = 0x3D123D12u;   // bf16x2(0.0356774) = sqrt(2/pi) * 0.044715
+  const uint32_t k0 = 0x3F4C3F4Cu;   // bf16x2(0.7978846) = sqrt(2/pi)
+  const uint32_t half = 0x3F003F00u; // bf16x2(0.5)
+  asm("mul.rn.bf16x2 %0, %1, %1;" : "=r"(sq) : "r"(x));
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(t) : "r"(sq), "r"(k1), "r"(k0));
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(u) : "r"(x), "r"(t));
+  asm("tanh.approx.bf16x2 %0, %1;" : "=r"(th) : "r"(u));
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(hx) : "r"(x), "r"(half));
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(g) : "r"(hx), "r"(th), "r"(hx));
+  return g;
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
