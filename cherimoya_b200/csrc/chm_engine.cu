@@ -1,6 +1,7 @@
 // chm_engine.cu -- C ABI of the Cherimoya B200 engine (see
 // include/cherimoya_b200.h). Host orchestration only: validation, workspace
 // carving, kernel dispatch. No entry point allocates device memory.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -92,15 +93,22 @@ Dims dims_of(const chm_model_desc* d) {
 
 // ---- packed weight buffer layout
 struct PackLayout {
-  size_t stem_w, stem_b, layers, layer_stride, l_convw, l_w1, l_w2;
-  size_t head_f, head_fb, head_lw, head_lb, total;
+  size_t stem_w, stem_b, stem_pk, layers, layer_stride, l_convw, l_w1, l_w2;
+  size_t head_f, head_fb, head_lw, head_lb, head_pk, total;
 };
+
+// channel width of the head's GEMM operand (a divisor-friendly padding)
+int head_cph(const Dims& m) {
+  const int cin = m.C + m.n_ctl;
+  return cin <= 64 ? 64 : (cin <= 128 ? 128 : 256);
+}
 
 PackLayout pack_layout(const Dims& m) {
   PackLayout p;
   size_t o = 0;
   p.stem_w = o; o = align_up(o + (size_t)m.C * 4 * kStemTaps * 4);
   p.stem_b = o; o = align_up(o + (size_t)m.C * 4);
+  p.stem_pk = o; o = align_up(o + 2 * (size_t)m.CP * sm::kK * 2);
   p.l_convw = 0;
   p.l_w1 = align_up(3 * (size_t)m.CP * 4);
   p.l_w2 = align_up(p.l_w1 + (size_t)m.HP * m.CP * 2);
@@ -111,6 +119,7 @@ PackLayout pack_layout(const Dims& m) {
   p.head_fb = o; o = align_up(o + (size_t)m.n_out * 4);
   p.head_lw = o; o = align_up(o + (size_t)m.n_groups * (m.C + (m.n_ctl > 0 ? 1 : 0)) * 4);
   p.head_lb = o; o = align_up(o + (size_t)m.n_groups * 4);
+  p.head_pk = o; o = align_up(o + (size_t)m.n_out * 2 * hd::kNP * head_cph(m) * 2);
   p.total = o;
   return p;
 }
@@ -157,6 +166,45 @@ int launch_status() {
     if (_s != CHM_OK) return _s;   \
   } while (0)
 
+// ---- TMA tensor maps (driver entry point resolved through the runtime, so
+// the library does not link libcuda directly)
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// Activation matrix (rows, CP) as a 2-D tensor of 128-byte x 128-row boxes
+// with the 128-byte swizzle; out-of-range rows read as zero.
+int make_act_tmap(CUtensorMap* map, const void* base, long long rows, int CP, int elem_bytes) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn) return CHM_ERR_CUDA;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return CHM_ERR_WORKSPACE;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(CP), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(CP) * elem_bytes};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / elem_bytes), 128u};
+  const cuuint32_t estr[2] = {1u, 1u};
+  const CUresult r = fn(map, elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                             : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                        2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? CHM_OK : CHM_ERR_CUDA;
+}
+
 // ---- MLP kernel dispatch over (act_t, CP, HP)
 template <typename act_t, int CP, int HP>
 int launch_mlp_t(const MlpArgs& a, int grid, cudaStream_t st, bool fast) {
@@ -179,15 +227,17 @@ int launch_mlp(const Dims& m, const MlpArgs& a, int grid, cudaStream_t st) {
   const bool fast = (m.mode == CHM_MODE_BF16);
   if (m.CP == ws::kC && m.HP == ws::kH) {
     const int smem = ws::kAlloc;
+    CUtensorMap tmap;
+    CHM_TRY(make_act_tmap(&tmap, a.X_in, a.rows, m.CP, sizeof(act_t)));
     LaunchTimer timer(kKMlp, st);
     if (fast) {
       auto k = mlp_ws_kernel<act_t, true>;
       cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      k<<<grid, ws::kThreads, smem, st>>>(a);
+      k<<<grid, ws::kThreads, smem, st>>>(a, tmap);
     } else {
       auto k = mlp_ws_kernel<act_t, false>;
       cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      k<<<grid, ws::kThreads, smem, st>>>(a);
+      k<<<grid, ws::kThreads, smem, st>>>(a, tmap);
     }
     return launch_status();
   }
@@ -240,23 +290,34 @@ int run_forward_t(const Dims& m, const PackLayout& pl, const uint8_t* packed, in
   act_t* xb = reinterpret_cast<act_t*>(ws + f.xb);
   if (cudaMemsetAsync(counters, 0, (size_t)batch * 4, st) != cudaSuccess) return CHM_ERR_CUDA;
 
-  // stem
+  // stem (tcgen05 im2col GEMM)
+  const long long rows = (long long)batch * m.L;
+  const int n_tiles = static_cast<int>((rows + kTileRows - 1) / kTileRows);
   {
-    dim3 grid((m.L + kStemL - 1) / kStemL, batch);
-    const float* w = reinterpret_cast<const float*>(packed + pl.stem_w);
     const float* bias = reinterpret_cast<const float*>(packed + pl.stem_b);
+    const uint8_t* wpk = packed + pl.stem_pk;
+    const bool split = (kIn == kInDense) && m.mode == CHM_MODE_FP32;
+    const int smem = stem_smem_bytes(m.CP, split ? 2 : 1);
+    const int sgrid = std::min(n_tiles, 2 * device_sms());
     LaunchTimer timer(kKStem, st);
-    if (kIn == kInDense)
-      stem_kernel<act_t, kInDense><<<grid, m.CP, 0, st>>>(in, w, bias, xa, m.L, m.C, m.CP);
-    else if (kIn == kInBases)
-      stem_kernel<act_t, kInBases><<<grid, m.CP, 0, st>>>(in, w, bias, xa, m.L, m.C, m.CP);
-    else
-      stem_kernel<act_t, kInIsm><<<grid, m.CP, 0, st>>>(in, w, bias, xa, m.L, m.C, m.CP);
+#define CHM_STEM(KIN, SPLITS)                                                             \
+  do {                                                                                    \
+    auto k = stem_mma_kernel<act_t, KIN, SPLITS>;                                         \
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);           \
+    k<<<sgrid, sm::kThreads, smem, st>>>(in, wpk, bias, xa, rows, m.L, m.C, m.CP, n_tiles, \
+                                         status);                                         \
+  } while (0)
+    if (kIn == kInDense) {
+      if (split) CHM_STEM(kInDense, 2); else CHM_STEM(kInDense, 1);
+    } else if (kIn == kInBases) {
+      CHM_STEM(kInBases, 1);
+    } else {
+      CHM_STEM(kInIsm, 1);
+    }
+#undef CHM_STEM
     CHM_TRY(launch_status());
   }
   // block stack
-  const long long rows = (long long)batch * m.L;
-  const int n_tiles = static_cast<int>((rows + kTileRows - 1) / kTileRows);
   const int grid = std::min(n_tiles, device_sms());
   for (int i = 0; i < m.n_layers; ++i) {
     const uint8_t* lw = packed + pl.layers + pl.layer_stride * i;
@@ -280,26 +341,54 @@ int run_forward_t(const Dims& m, const PackLayout& pl, const uint8_t* packed, in
     std::swap(xa, xb);
   }
   // heads
-  {
+  const int cph = head_cph(m);
+  const bool split_a = (m.mode == CHM_MODE_FP32);
+  if (!(cph == 256 && split_a)) {
+    HeadArgs h;
+    h.status = status;
+    h.X = xa;
+    h.X_ctl = x_ctl;
+    h.fb = packed + pl.head_pk;
+    h.fbias = reinterpret_cast<const float*>(packed + pl.head_fb);
+    h.lw = reinterpret_cast<const float*>(packed + pl.head_lw);
+    h.lbias = reinterpret_cast<const float*>(packed + pl.head_lb);
+    h.profile = profile;
+    h.logcounts = logcounts;
+    h.L = m.L; h.C = m.C; h.CP = m.CP; h.CPH = cph; h.n_ctl = m.n_ctl; h.n_out = m.n_out;
+    h.n_groups = m.n_groups; h.T = m.T; h.Lout = m.Lout;
+    const int smem = head_smem_bytes(cph, split_a ? 2 : 1);
+    dim3 hgrid(m.n_out, batch);
+    LaunchTimer timer(kKProfile, st);
+    if (split_a) {
+      auto k = head_kernel<act_t, 2>;
+      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      k<<<hgrid, hd::kThreads, smem, st>>>(h);
+    } else {
+      auto k = head_kernel<act_t, 1>;
+      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      k<<<hgrid, hd::kThreads, smem, st>>>(h);
+    }
+    CHM_TRY(launch_status());
+  } else {
     const int cin = m.C + m.n_ctl;
     const int smem = (cin * kHeadWin + kHeadWarps * kHeadJ) * 4;
     auto k = profile_head_kernel<act_t>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     dim3 grid_h((m.Lout + kHeadJ - 1) / kHeadJ, batch);
     {
-    LaunchTimer timer(kKProfile, st);
-    k<<<grid_h, kHeadWarps * 32, smem, st>>>(
-        xa, x_ctl, reinterpret_cast<const float*>(packed + pl.head_f),
-        reinterpret_cast<const float*>(packed + pl.head_fb), profile, m.L, m.C, m.CP, m.n_ctl,
-        m.n_out, m.T, m.Lout);
+      LaunchTimer timer(kKProfile, st);
+      k<<<grid_h, kHeadWarps * 32, smem, st>>>(
+          xa, x_ctl, reinterpret_cast<const float*>(packed + pl.head_f),
+          reinterpret_cast<const float*>(packed + pl.head_fb), profile, m.L, m.C, m.CP, m.n_ctl,
+          m.n_out, m.T, m.Lout);
     }
     CHM_TRY(launch_status());
     {
-    LaunchTimer timer(kKCount, st);
-    count_head_kernel<act_t><<<batch, 256, 0, st>>>(
-        xa, x_ctl, reinterpret_cast<const float*>(packed + pl.head_lw),
-        reinterpret_cast<const float*>(packed + pl.head_lb), logcounts, m.L, m.C, m.CP, m.n_ctl,
-        m.n_groups, m.T);
+      LaunchTimer timer(kKCount, st);
+      count_head_kernel<act_t><<<batch, 256, 0, st>>>(
+          xa, x_ctl, reinterpret_cast<const float*>(packed + pl.head_lw),
+          reinterpret_cast<const float*>(packed + pl.head_lb), logcounts, m.L, m.C, m.CP,
+          m.n_ctl, m.n_groups, m.T);
     }
     CHM_TRY(launch_status());
   }
@@ -327,7 +416,10 @@ int validate(const chm_model_desc* d) {
   const Dims m = dims_of(d);
   if (m.CP > 128 || m.HP > 256) return CHM_ERR_UNSUPPORTED;
   const int cin = m.C + m.n_ctl;
-  if ((cin * kHeadWin + kHeadWarps * kHeadJ) * 4 > 227 * 1024) return CHM_ERR_UNSUPPORTED;
+  if (cin > 256) return CHM_ERR_UNSUPPORTED;
+  if ((cin * kHeadWin + kHeadWarps * kHeadJ) * 4 > 227 * 1024 && head_cph(m) == 256 &&
+      m.mode == CHM_MODE_FP32)
+    return CHM_ERR_UNSUPPORTED;
   return CHM_OK;
 }
 
@@ -498,6 +590,9 @@ int32_t chm_pack_weights(const chm_model_desc* desc, const chm_params* p, void* 
     return launch_status();
   };
   CHM_TRY(copy(p->iconv_weight, pl.stem_w, (long long)m.C * 4 * kStemTaps));
+  pack_sw128_split_kernel<<<(m.CP * sm::kK + 255) / 256, 256, 0, st>>>(
+      p->iconv_weight, m.C, 4 * kStemTaps, m.CP, sm::kK, dst + pl.stem_pk);
+  CHM_TRY(launch_status());
   CHM_TRY(copy(p->iconv_bias, pl.stem_b, m.C));
   for (int i = 0; i < m.n_layers; ++i) {
     if (!p->conv_weight[i] || !p->linear1_weight[i] || !p->linear2_weight[i])
@@ -518,6 +613,12 @@ int32_t chm_pack_weights(const chm_model_desc* desc, const chm_params* p, void* 
   const long long cin = (long long)m.C + m.n_ctl;
   CHM_TRY(copy(p->fconv_weight, pl.head_f, (long long)m.n_out * cin * kHeadTaps));
   CHM_TRY(copy(p->fconv_bias, pl.head_fb, m.n_out));
+  {
+    const long long n = (long long)m.n_out * hd::kNP * head_cph(m);
+    pack_head_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
+        p->fconv_weight, m.n_out, (int)cin, kHeadTaps, hd::kNP, head_cph(m), dst + pl.head_pk);
+    CHM_TRY(launch_status());
+  }
   CHM_TRY(copy(p->linear_weight, pl.head_lw,
                (long long)m.n_groups * (m.C + (m.n_ctl > 0 ? 1 : 0))));
   CHM_TRY(copy(p->linear_bias, pl.head_lb, m.n_groups));

@@ -5,6 +5,7 @@
 // multiple of 64; padded channels hold 0). act_t is float (fp32 mode) or
 // __nv_bfloat16 (bf16 mode).
 #pragma once
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cstdint>
 #include <type_traits>
@@ -156,6 +157,18 @@ __device__ __forceinline__ uint4 add_residual(const uint4& x, const uint32_t* d)
   }
 }
 
+__host__ __device__ __forceinline__ int kHeadThreadsRows(int chunks) { return 128 / chunks; }
+
+template <typename act_t>
+__device__ __forceinline__ void unpack_chunk(const uint4& t, float (&v)[16 / sizeof(act_t)]) {
+  if constexpr (sizeof(act_t) == 2) {
+    unpack8(t, v);
+  } else {
+    v[0] = __uint_as_float(t.x); v[1] = __uint_as_float(t.y);
+    v[2] = __uint_as_float(t.z); v[3] = __uint_as_float(t.w);
+  }
+}
+
 // ============================================================== input
 // Input of the stem, one of:
 //  kInDense : x (B, 4, L) fp32 or bf16 (NCL), any values
@@ -256,6 +269,157 @@ __global__ void __launch_bounds__(256) stem_kernel(StemInput in, const float* __
                               : 0.f;
       X[((long long)b * L + l) * CP + c] = from_f32<act_t>(y);
     }
+  }
+}
+
+// ============================================================== stem, tcgen05
+// Stem as an im2col GEMM over 128-row tiles of the flattened (B*L) rows:
+//   A[r, 21k + t] = x[b, k, l + t - 10]  (K = 84, padded to 128, zero pad)
+//   X0[r, c] = gelu_tanh(bias[c] + sum_kk A[r, kk] W[c, kk])
+// (upstream cherimoya.py:173-174, 373). W is packed as bf16 hi + lo (two
+// MMAs carry it to ~16 bits); one-hot / base inputs are exact in bf16, a
+// dense fp32 input is split into hi + lo as well (third MMA).
+namespace sm {
+constexpr int kK = 128;            // padded im2col width
+constexpr int kThreads = 128;
+}  // namespace sm
+
+__host__ __device__ constexpr uint32_t stem_smem_bytes(int CP, int a_splits) {
+  return static_cast<uint32_t>(2 * CP * sm::kK * 2 + a_splits * kTileRows * sm::kK * 2 + 64 +
+                               1024);
+}
+
+template <typename act_t, int kIn, int kASplits>
+__global__ void __launch_bounds__(sm::kThreads) stem_mma_kernel(StemInput in,
+                                                                const uint8_t* __restrict__ wpk,
+                                                                const float* __restrict__ bias,
+                                                                act_t* X, long long rows, int L,
+                                                                int C, int CP, int n_tiles,
+                                                                int* status) {
+  using namespace sm;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sB = smem;                                 // [hi | lo] CP x 128
+  uint8_t* sA = sB + 2 * CP * kK * 2;                 // [kASplits] 128 x 128
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sA + kASplits * kTileRows * kK * 2);
+  uint32_t* slot = reinterpret_cast<uint32_t*>(bar + 1);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (warp == 0) tmem_alloc(slot, 256);
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    mbar_init_fence();
+  }
+  {
+    const uint4* g = reinterpret_cast<const uint4*>(wpk);
+    uint4* d = reinterpret_cast<uint4*>(sB);
+    for (int i = tid; i < 2 * CP * kK * 2 / 16; i += blockDim.x) d[i] = g[i];
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *slot;
+  const uint32_t sA_addr = smem_u32(sA), sB_addr = smem_u32(sB);
+  const uint32_t idesc = idesc_bf16(kTileRows, CP);
+  const uint32_t lane_sel = static_cast<uint32_t>(warp * 32) << 16;
+  uint32_t it = 0;
+  for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+    const long long r = (long long)tile * kTileRows + tid;   // thread = tile row
+    const bool rv = r < rows;
+    const int b = rv ? static_cast<int>(r / L) : 0;
+    const int l = rv ? static_cast<int>(r - (long long)b * L) : 0;
+    // ---- im2col row -> A (hi [, lo]); element kk = 21k + t
+    uint8_t* sAlo = sA + kTileRows * kK * 2;
+#pragma unroll 1
+    for (int t = 0; t < kStemTaps; ++t) {
+      float col[4] = {0.f, 0.f, 0.f, 0.f};
+      const int p = l + t - kStemPad;
+      if (rv && p >= 0 && p < L) stem_column<kIn>(in, L, b, p, col);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t off = sw128_offset(tid, 21 * k + t, kTileRows);
+        const __nv_bfloat16 h = __float2bfloat16_rn(col[k]);
+        *reinterpret_cast<__nv_bfloat16*>(sA + off) = h;
+        if (kASplits > 1)
+          *reinterpret_cast<__nv_bfloat16*>(sAlo + off) =
+              __float2bfloat16_rn(col[k] - __bfloat162float(h));
+      }
+    }
+    // zero padding kk = 84 .. 127 (rows written by their own thread)
+    for (int kk = 84; kk < kK; ++kk) {
+      *reinterpret_cast<__nv_bfloat16*>(sA + sw128_offset(tid, kk, kTileRows)) =
+          __float2bfloat16_rn(0.f);
+      if (kASplits > 1)
+        *reinterpret_cast<__nv_bfloat16*>(sA + kTileRows * kK * 2 +
+                                          sw128_offset(tid, kk, kTileRows)) =
+            __float2bfloat16_rn(0.f);
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      uint32_t acc = 0;
+      for (int term = 0; term < (kASplits > 1 ? 3 : 2); ++term) {
+        const int ai = (term == 2) ? 1 : 0;
+        const int bi = (term == 1) ? 1 : 0;
+#pragma unroll
+        for (int kk = 0; kk < kK / 16; ++kk) {
+          const uint64_t da = desc_sw128(sA_addr + ai * (kTileRows * kK * 2) +
+                                         (kk >> 2) * (kTileRows * 128) + (kk & 3) * 32);
+          const uint64_t db = desc_sw128(sB_addr + bi * (CP * kK * 2) + (kk >> 2) * (CP * 128) +
+                                         (kk & 3) * 32);
+          mma_bf16(tmem, da, db, idesc, acc);
+          acc = 1;
+        }
+      }
+      mma_commit(bar);
+    }
+    const bool ok = mbar_wait(bar, it & 1);
+    if (__syncthreads_or(!ok)) {
+      if (tid == 0) atomicExch(status, kStatusTimeout);
+      break;
+    }
+    tc_fence_after();
+    // ---- bias + GELU -> X0 row
+#pragma unroll 1
+    for (int j = 0; j < CP / 32; ++j) {
+      uint32_t d[32];
+      tmem_ld32(tmem + lane_sel + j * 32, d);
+      tmem_ld_wait();
+      if (rv) {
+        float y[32];
+#pragma unroll
+        for (int q = 0; q < 32; ++q) {
+          const int c = j * 32 + q;
+          const float z = __uint_as_float(d[q]) + (c < C ? bias[c] : 0.f);
+          y[q] = (c < C) ? gelu_tanh<sizeof(act_t) == 2>(z) : 0.f;
+        }
+        act_t* dst = X + r * CP + j * 32;
+        if constexpr (sizeof(act_t) == 2) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4*>(dst + q * 8) =
+                make_uint4(pack_bf16x2(y[8 * q], y[8 * q + 1]), pack_bf16x2(y[8 * q + 2], y[8 * q + 3]),
+                           pack_bf16x2(y[8 * q + 4], y[8 * q + 5]),
+                           pack_bf16x2(y[8 * q + 6], y[8 * q + 7]));
+        } else {
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<float4*>(dst + q * 4) =
+                make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
+        }
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
   }
 }
 
@@ -676,37 +840,53 @@ __global__ void __launch_bounds__(128, 1) mlp_kernel(MlpArgs a) {
 // ============================================================== MLP, pipelined
 // Warp-specialised persistent version of mlp_kernel for the default width
 // (C = 128, H = 256). Roles, per CTA (one CTA per SM):
-//   warps 0-3  producer : conv + LayerNorm of tile t -> A1 (bf16, swizzled)
-//   warps 4-11 epilogue : GELU of D1 halves -> A2a / A2b, residual of D2
-//   warp 12    MMA      : one elected thread issues all tcgen05.mma
-// H is split in halves (a: h 0..127, b: h 128..255) so the GELU of one half
-// overlaps the MMAs of the other. The tensor pipe runs, per tile t,
-//   G2a(t)  G1a(t+1)  G2b(t)  G1b(t+1)
-// with G1x: D1x = A1 * W1[x]^T and G2x: D2 (+)= A2x * W2[:, x]^T.
-// TMEM (512 columns): D1a | D1b | D2[0] | D2[1] (D2 double-buffered so the
-// residual of tile t overlaps the MMAs of tile t+1).
-// Shared memory: W1 64 KB + W2 64 KB (resident), A1 32 KB, A2a + A2b 64 KB.
+//   warps 0-3   producer : TMA loads of the three row blocks a tile's conv
+//                          reads (rows - d, rows, rows + d) into a swizzled
+//                          staging buffer; conv + LayerNorm (thread = row);
+//                          bf16 result written into TMEM (A operand of GEMM1)
+//   warps 4-11  epilogue : GELU of the D1 halves, written back into TMEM as
+//                          bf16 (A operand of GEMM2); residual of D2
+//   warp 12     MMA      : one elected thread issues all tcgen05.mma
+// H is split in halves (a: h 0..127, b: h 128..255). G1x: D1x = A1 * W1[x]^T,
+// G2x: D2 (+)= gelu(D1x) * W2[:, x]^T; both take A from TMEM. MMAs issued by
+// one thread execute in order, so G1x(t+1) overwriting D1x cannot overtake
+// G2x(t) reading it. After G2a(t) the issuer takes G2b(t) or G1a(t+1),
+// whichever is ready first.
+// TMEM (512 columns): D1a [0,128) | D1b [128,256) | D2 [256,384) |
+// A1[0] [384,448) | A1[1] [448,512). The bf16 GELU output of half x lives in
+// D1x's own columns: epilogue warpgroup g packs h [64g, 64g+64) of the half
+// into columns [64g, 64g+32), which it has already read.
+// Shared memory: W1 64 KB + W2 64 KB (resident), staging 2 slots x 48 KB
+// (each: the three row blocks of one 128-byte channel box, 128 rows each),
+// conv weights. A tile is processed box by box (2 boxes of 64 bf16 channels,
+// or 4 of 32 fp32 channels); the TMA for box step k + 2 is issued as soon as
+// box step k has been consumed, so loads overlap the conv of the next box.
 namespace ws {
 constexpr int kC = 128, kH = 256, kHalf = 128;
 constexpr int kProducerWarps = 4, kEpilogueWarps = 8;
 constexpr int kMmaWarp = kProducerWarps + kEpilogueWarps;      // 12
 constexpr int kThreads = (kMmaWarp + 1) * 32;                   // 416
+constexpr uint32_t kBox = 128 * 128;                            // 16 KB TMA box
 constexpr uint32_t kW1 = 0;                                     // 256 x 128 bf16
 constexpr uint32_t kW2 = kW1 + kH * kC * 2;                     // 128 x 256 bf16
-constexpr uint32_t kA1 = kW2 + kC * kH * 2;                     // 128 x 128
-constexpr uint32_t kA2a = kA1 + kTileRows * kC * 2;             // 128 x 128
-constexpr uint32_t kA2b = kA2a + kTileRows * kHalf * 2;         // 128 x 128
-constexpr uint32_t kBars = kA2b + kTileRows * kHalf * 2;
-enum Bar { A1_FULL, A1_EMPTY, D1A_FULL, D1B_FULL, A2A_FULL, A2B_FULL, A2A_EMPTY, A2B_EMPTY,
-           D2_FULL0, D2_FULL1, D2_EMPTY0, D2_EMPTY1, kNumBars };
+constexpr uint32_t kStg = kW2 + kC * kH * 2;                    // 2 slots x 3 boxes
+constexpr uint32_t kSlotBytes = 3 * kBox;
+constexpr uint32_t kConvW = kStg + 2 * kSlotBytes;              // 3 x 128 fp32
+constexpr uint32_t kBars = kConvW + 3 * kC * 4;
+enum Bar { STG_FULL0, STG_FULL1, STG_EMPTY0, STG_EMPTY1, A1_FULL0, A1_FULL1, A1_EMPTY0,
+           A1_EMPTY1, D1A_FULL, D1B_FULL, A2A_FULL, A2B_FULL, D2_FULL, kNumBars };
 constexpr uint32_t kSlot = kBars + kNumBars * 8;
 constexpr uint32_t kAbort = kSlot + 4;
 constexpr uint32_t kBytes = kAbort + 4;
 constexpr uint32_t kAlloc = kBytes + 1024;
+constexpr uint32_t kD2Col = 256, kA1Col = 384;
+// TMEM column of the packed bf16 A2 for K-step s (16 h values) of a half
+__host__ __device__ constexpr uint32_t a2_col(int s) { return s < 4 ? 8 * s : 64 + 8 * (s - 4); }
 }  // namespace ws
 
 template <typename act_t, bool kFastGelu>
-__global__ void __launch_bounds__(ws::kThreads, 1) mlp_ws_kernel(MlpArgs a) {
+__global__ void __launch_bounds__(ws::kThreads, 1)
+    mlp_ws_kernel(MlpArgs a, const __grid_constant__ CUtensorMap tmap_x) {
   using namespace ws;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -714,15 +894,18 @@ __global__ void __launch_bounds__(ws::kThreads, 1) mlp_ws_kernel(MlpArgs a) {
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBars);
   uint32_t* slot = reinterpret_cast<uint32_t*>(smem + kSlot);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kAbort);
+  const float* sConvW = reinterpret_cast<const float*>(smem + kConvW);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const act_t* Xi = static_cast<const act_t*>(a.X_in);
   act_t* Xo = static_cast<act_t*>(a.X_out);
+  constexpr int kBoxCh = 128 / sizeof(act_t);                   // channels per TMA box
+  constexpr int kBoxes = kC / kBoxCh;                           // box steps per tile
 
   if (warp == kMmaWarp) tmem_alloc(slot, 512);
   if (tid == 0) {
-    const uint32_t counts[kNumBars] = {kProducerWarps * 32, 1, 1, 1, kEpilogueWarps * 32,
-                                       kEpilogueWarps * 32, 1, 1, 1, 1, kEpilogueWarps * 32,
-                                       kEpilogueWarps * 32};
+    const uint32_t counts[kNumBars] = {1, 1, kProducerWarps * 32, kProducerWarps * 32,
+                                       kProducerWarps * 32, kProducerWarps * 32, 1, 1, 1, 1,
+                                       kEpilogueWarps * 32, kEpilogueWarps * 32, 1};
     for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], counts[i]);
     *abort_flag = 0;
     mbar_init_fence();
@@ -734,6 +917,11 @@ __global__ void __launch_bounds__(ws::kThreads, 1) mlp_ws_kernel(MlpArgs a) {
     uint4* s2 = reinterpret_cast<uint4*>(smem + kW2);
     for (int i = tid; i < kH * kC * 2 / 16; i += blockDim.x) s1[i] = g1[i];
     for (int i = tid; i < kC * kH * 2 / 16; i += blockDim.x) s2[i] = g2[i];
+    float* cw = reinterpret_cast<float*>(smem + kConvW);
+    for (int i = tid; i < 3 * kC; i += blockDim.x) {
+      const int c = i % kC;
+      cw[i] = (c < a.C) ? a.convw[i] : 0.f;
+    }
   }
   fence_async_smem();
   tc_fence_before();
@@ -746,92 +934,140 @@ __global__ void __launch_bounds__(ws::kThreads, 1) mlp_ws_kernel(MlpArgs a) {
 
   if (warp < kProducerWarps) {
     // ------------------------------------------------------------ producer
-    // lane pair (i, i+16) covers two rows; each lane 8 channels (16 B bf16)
-    constexpr int CPL = 8;
-    const int rsel = lane >> 4;
-    const int c0 = (lane & 15) * CPL;
-    float cw0[CPL], cw1[CPL], cw2[CPL];
+    const int quarter = warp & 3;                 // TMEM lane quarter = tile rows
+    const int rl = quarter * 32 + lane;           // tile row of this thread
+    const uint32_t lane_sel = static_cast<uint32_t>(quarter * 32) << 16;
+    // box step k -> (tile it = k / kBoxes, box b = k % kBoxes) into slot k & 1
+    auto issue = [&](uint32_t k) {
+      const int tit = static_cast<int>(k / kBoxes);
+      if (tit >= n_my) return;
+      const int b = static_cast<int>(k % kBoxes);
+      const int slotk = k & 1;
+      const int y0 = (first + tit * stride) * kTileRows;
+      mbar_expect_tx(&bars[STG_FULL0 + slotk], kSlotBytes);
 #pragma unroll
-    for (int j = 0; j < CPL; ++j) {
-      const bool live = c0 + j < a.C;
-      cw0[j] = live ? a.convw[c0 + j] : 0.f;
-      cw1[j] = live ? a.convw[kC + c0 + j] : 0.f;
-      cw2[j] = live ? a.convw[2 * kC + c0 + j] : 0.f;
+      for (int blk = 0; blk < 3; ++blk)
+        tma_load_2d(smem + kStg + (slotk * 3 + blk) * kBox, &tmap_x, b * kBoxCh,
+                    y0 + (blk - 1) * a.dil, &bars[STG_FULL0 + slotk]);
+    };
+    if (tid == 0) {
+      issue(0);
+      issue(1);
     }
-    using raw_t = typename std::conditional<sizeof(act_t) == 2, uint4, Raw8f>::type;
-    constexpr int kU = sizeof(act_t) == 2 ? 4 : 2;  // row pairs in flight per thread
-    uint8_t* sA1 = smem + kA1;
-    for (int it = 0; it < n_my; ++it) {
+    uint32_t k = 0;
+    bool ok = true;
+    for (int it = 0; it < n_my && ok; ++it) {
+      const int buf = it & 1;
       const long long row0 = (long long)(first + it * stride) * kTileRows;
-      bool waited = false;
-      for (int p0 = 0; p0 < 16; p0 += kU) {
-        raw_t xc[kU], xl[kU], xr[kU];
-        float2 st[kU];
-#pragma unroll
-        for (int u = 0; u < kU; ++u) {
-          const long long r = row0 + warp * 32 + (p0 + u) * 2 + rsel;
-          xc[u] = raw_t{}; xl[u] = raw_t{}; xr[u] = raw_t{};
-          st[u] = make_float2(0.f, 0.f);
-          if (r < a.rows) {
-            const int n = static_cast<int>(r / a.L);
-            const int l = static_cast<int>(r - (long long)n * a.L);
-            st[u] = a.stats[n];
-            xc[u] = ldraw<raw_t>(Xi + r * kC + c0);
-            if (l - a.dil >= 0) xl[u] = ldraw<raw_t>(Xi + (r - a.dil) * kC + c0);
-            if (l + a.dil < a.L) xr[u] = ldraw<raw_t>(Xi + (r + a.dil) * kC + c0);
-          }
-        }
-        // the first batch of loads is in flight before waiting for the buffer
-        if (!waited) {
-          if (!mbar_wait_abortable(&bars[A1_EMPTY], (it & 1) ^ 1, abort_flag)) break;
-          waited = true;
-        }
-#pragma unroll
-        for (int u = 0; u < kU; ++u) {
-          float fc[CPL], fl[CPL], fr[CPL];
-          unpack8(xc[u], fc);
-          unpack8(xl[u], fl);
-          unpack8(xr[u], fr);
-          float v[CPL];
-          const float shift = -st[u].x * st[u].y;
-#pragma unroll
-          for (int j = 0; j < CPL; ++j) {
-            const float y = fmaf(cw0[j], fl[j], fmaf(cw1[j], fc[j], cw2[j] * fr[j]));
-            v[j] = fmaf(y, st[u].y, shift);
-          }
-          const int rl = warp * 32 + (p0 + u) * 2 + rsel;
-          *reinterpret_cast<uint4*>(sA1 + sw128_offset(rl, c0, kTileRows)) =
-              make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
-                         pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
-        }
+      const long long r = row0 + rl;
+      const bool rv = r < a.rows;
+      int l = 0;
+      float2 st = make_float2(0.f, 0.f);
+      if (rv) {
+        const int n = static_cast<int>(r / a.L);
+        l = static_cast<int>(r - (long long)n * a.L);
+        st = a.stats[n];
       }
-      if (!waited) break;
-      fence_async_smem();
-      mbar_arrive(&bars[A1_FULL]);
+      const f2 scale2{st.y, st.y};
+      const f2 shift2{-st.x * st.y, -st.x * st.y};
+      const bool hasL = rv && (l - a.dil >= 0), hasR = rv && (l + a.dil < a.L);
+      for (int b = 0; b < kBoxes; ++b, ++k) {
+        const int slotk = k & 1;
+        ok = mbar_wait_abortable(&bars[STG_FULL0 + slotk], (k >> 1) & 1, abort_flag);
+        if (!ok) break;
+        if (b == 0) {
+          ok = mbar_wait_abortable(&bars[A1_EMPTY0 + buf], ((it >> 1) & 1) ^ 1, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+        }
+        // conv + LayerNorm of this thread's row over the box's channels
+        const uint8_t* bL = smem + kStg + (slotk * 3 + 0) * kBox + rl * 128;
+        const uint8_t* bC = bL + kBox;
+        const uint8_t* bR = bL + 2 * kBox;
+        const int cbase = b * kBoxCh;              // first channel of the box
+        uint32_t packed[kBoxCh / 2];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {              // 16-byte chunks of the row
+          const uint32_t off = static_cast<uint32_t>((q ^ (rl & 7)) * 16);
+          uint4 vl = *reinterpret_cast<const uint4*>(bL + off);
+          const uint4 vc = *reinterpret_cast<const uint4*>(bC + off);
+          uint4 vr = *reinterpret_cast<const uint4*>(bR + off);
+          if (!hasL) vl = make_uint4(0, 0, 0, 0);
+          if (!hasR) vr = make_uint4(0, 0, 0, 0);
+          constexpr int kE = 16 / sizeof(act_t);  // elements per chunk
+          float fl[kE], fc[kE], fr[kE];
+          unpack_chunk<act_t>(vl, fl);
+          unpack_chunk<act_t>(vc, fc);
+          unpack_chunk<act_t>(vr, fr);
+          const int c = cbase + q * kE;
+#pragma unroll
+          for (int e = 0; e < kE; e += 4) {
+            const float4 w0 = *reinterpret_cast<const float4*>(sConvW + c + e);
+            const float4 w1 = *reinterpret_cast<const float4*>(sConvW + kC + c + e);
+            const float4 w2 = *reinterpret_cast<const float4*>(sConvW + 2 * kC + c + e);
+            f2 y0 = mul2(f2{w2.x, w2.y}, f2{fr[e], fr[e + 1]});
+            f2 y1 = mul2(f2{w2.z, w2.w}, f2{fr[e + 2], fr[e + 3]});
+            y0 = fma2(f2{w1.x, w1.y}, f2{fc[e], fc[e + 1]}, y0);
+            y1 = fma2(f2{w1.z, w1.w}, f2{fc[e + 2], fc[e + 3]}, y1);
+            y0 = fma2(f2{w0.x, w0.y}, f2{fl[e], fl[e + 1]}, y0);
+            y1 = fma2(f2{w0.z, w0.w}, f2{fl[e + 2], fl[e + 3]}, y1);
+            y0 = fma2(y0, scale2, shift2);
+            y1 = fma2(y1, scale2, shift2);
+            packed[(q * kE + e) / 2] = pack_bf16x2(y0.x, y0.y);
+            packed[(q * kE + e) / 2 + 1] = pack_bf16x2(y1.x, y1.y);
+          }
+        }
+        if (!rv) {
+#pragma unroll
+          for (int e = 0; e < kBoxCh / 2; ++e) packed[e] = 0u;
+        }
+        // staging consumed: release the slot; thread 0 refills it (box k + 2).
+        // The proxy fence orders these generic-proxy reads before the TMA
+        // (async proxy) overwrites the slot; without it the refill can land
+        // before the reads complete.
+        fence_async_smem();
+        mbar_arrive(&bars[STG_EMPTY0 + slotk]);
+        if (tid == 0) {
+          ok = mbar_wait_abortable(&bars[STG_EMPTY0 + slotk], (k >> 1) & 1, abort_flag);
+          if (ok) issue(k + 2);
+        }
+        // packed channels [cbase, cbase + kBoxCh) -> A1 columns cbase / 2 ...
+        const uint32_t col = tmem + lane_sel + kA1Col + buf * 64 + cbase / 2;
+#pragma unroll
+        for (int h = 0; h < kBoxCh / 32; ++h) {
+          uint32_t pp[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) pp[e] = packed[h * 16 + e];
+          tmem_st16(col + h * 16, pp);
+        }
+        if (!ok) break;
+      }
+      if (!ok) break;
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&bars[A1_FULL0 + buf]);
     }
   } else if (warp < kMmaWarp) {
     // ------------------------------------------------------------ epilogue
     const int ew = warp - kProducerWarps;          // 0..7
     const int quarter = warp & 3;                  // TMEM lane quarter of this warp
-    const int colhalf = ew >> 2;                   // 0: columns 0-63, 1: 64-127
+    const int g = ew >> 2;                         // warpgroup: half columns [64g, 64g+64)
     const int rl = quarter * 32 + lane;            // tile row of this thread
     const uint32_t lane_sel = static_cast<uint32_t>(quarter * 32) << 16;
     for (int it = 0; it < n_my; ++it) {
       const long long row0 = (long long)(first + it * stride) * kTileRows;
       bool ok = true;
 #pragma unroll 1
-      for (int hh = 0; hh < 2 && ok; ++hh) {
-        // GELU of half hh: D1x -> A2x
-        ok = mbar_wait_abortable(&bars[hh ? D1B_FULL : D1A_FULL], it & 1, abort_flag) &&
-             mbar_wait_abortable(&bars[hh ? A2B_EMPTY : A2A_EMPTY], (it & 1) ^ 1, abort_flag);
+      for (int hh = 0; hh < 2; ++hh) {
+        // GELU of half hh, in place: D1x fp32 -> packed bf16 A2x
+        ok = mbar_wait_abortable(&bars[hh ? D1B_FULL : D1A_FULL], it & 1, abort_flag);
         if (!ok) break;
         tc_fence_after();
-        uint8_t* sA2 = smem + (hh ? kA2b : kA2a);
-        const uint32_t tcol = tmem + hh * kHalf + colhalf * 64;
+        const uint32_t base = tmem + lane_sel + hh * kHalf + g * 64;
 #pragma unroll 1
         for (int j = 0; j < 2; ++j) {
           uint32_t r[32];
-          tmem_ld32(tcol + lane_sel + j * 32, r);
+          tmem_ld32(base + j * 32, r);
           tmem_ld_wait();
           uint32_t p[16];
 #pragma unroll
@@ -843,117 +1079,122 @@ __global__ void __launch_bounds__(ws::kThreads, 1) mlp_ws_kernel(MlpArgs a) {
                                  gelu_tanh<false>(__uint_as_float(r[2 * q + 1])));
             }
           }
-          const int kbase = colhalf * 64 + j * 32;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            *reinterpret_cast<uint4*>(sA2 + sw128_offset(rl, kbase + q * 8, kTileRows)) =
-                make_uint4(p[4 * q], p[4 * q + 1], p[4 * q + 2], p[4 * q + 3]);
-          }
+          tmem_st16(base + j * 16, p);
         }
-        fence_async_smem();
+        tmem_st_wait();
         tc_fence_before();
         mbar_arrive(&bars[hh ? A2B_FULL : A2A_FULL]);
       }
       if (!ok) break;
-      // residual of D2[b]; the thread's input channels are fetched before the
+      // residual of D2; the thread's input channels are fetched before the
       // wait (they do not depend on the MMAs)
-      const int b = it & 1;
       const long long r = row0 + rl;
       const bool rv = r < a.rows;
       constexpr int kVE = 16 / sizeof(act_t);      // elements per 16-byte vector
       constexpr int kPre = 32 / kVE;                // vectors of one 32-column chunk
-      const act_t* xrow = Xi + r * kC + colhalf * 64;
-      act_t* orow = Xo + r * kC + colhalf * 64;
-      uint4 xin[kPre];
+      // bf16: both 32-column chunks prefetched (8 vectors); fp32: the first
+      constexpr int kPreAll = sizeof(act_t) == 2 ? 2 * kPre : kPre;
+      const act_t* xrow = Xi + r * kC + g * 64;
+      act_t* orow = Xo + r * kC + g * 64;
+      uint4 xin[kPreAll];
 #pragma unroll
-      for (int q = 0; q < kPre; ++q) xin[q] = rv ? *reinterpret_cast<const uint4*>(xrow + q * kVE)
-                                              : make_uint4(0, 0, 0, 0);
-      if (!mbar_wait_abortable(&bars[D2_FULL0 + b], (it >> 1) & 1, abort_flag)) break;
+      for (int q = 0; q < kPreAll; ++q)
+        xin[q] = rv ? *reinterpret_cast<const uint4*>(xrow + q * kVE) : make_uint4(0, 0, 0, 0);
+      if (!mbar_wait_abortable(&bars[D2_FULL], it & 1, abort_flag)) break;
       tc_fence_after();
-      const uint32_t tcol = tmem + 2 * kHalf + b * kC + colhalf * 64;
-#pragma unroll 1
+      const uint32_t tcol = tmem + kD2Col + g * 64;
+#pragma unroll
       for (int j = 0; j < 2; ++j) {
         uint32_t d[32];
         tmem_ld32(tcol + lane_sel + j * 32, d);
-        if (j == 1) {
+        if (kPreAll == kPre && j == 1) {
 #pragma unroll
           for (int q = 0; q < kPre; ++q)
-            xin[q] = rv ? *reinterpret_cast<const uint4*>(xrow + 32 + q * kVE)
-                        : make_uint4(0, 0, 0, 0);
+            xin[q % kPreAll] = rv ? *reinterpret_cast<const uint4*>(xrow + 32 + q * kVE)
+                                  : make_uint4(0, 0, 0, 0);
         }
         tmem_ld_wait();
         if (rv) {
 #pragma unroll
           for (int q = 0; q < kPre; ++q)
             *reinterpret_cast<uint4*>(orow + j * 32 + q * kVE) =
-                add_residual<act_t>(xin[q], d + q * kVE);
+                add_residual<act_t>(xin[(kPreAll == kPre) ? q : j * kPre + q], d + q * kVE);
         }
       }
+      // D2 is next written by G2a(t+1), which the MMA issues only after this
+      // warpgroup's GELU of tile t+1: program order protects it.
       tc_fence_before();
-      mbar_arrive(&bars[D2_EMPTY0 + b]);
     }
   } else {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && n_my > 0) {
-      const uint32_t sA1 = smem_u32(smem + kA1), sW1 = smem_u32(smem + kW1);
-      const uint32_t sW2 = smem_u32(smem + kW2);
-      const uint32_t sA2[2] = {smem_u32(smem + kA2a), smem_u32(smem + kA2b)};
+      const uint32_t sW1 = smem_u32(smem + kW1), sW2 = smem_u32(smem + kW2);
       constexpr uint32_t kIdesc = idesc_bf16(kTileRows, 128);
-      auto g1 = [&](int hh) {  // D1x = A1 * W1[hh*128 : hh*128+128]^T, K = 128
+      auto g1 = [&](int hh, int buf) {  // D1x = A1(tmem) * W1[hh*128 : hh*128+128]^T, K = 128
         const uint32_t d = tmem + hh * kHalf;
 #pragma unroll
         for (int k = 0; k < kC / 16; ++k) {
-          const uint64_t da = desc_sw128(sA1 + (k >> 2) * (kTileRows * 128) + (k & 3) * 32);
           const uint64_t db =
               desc_sw128(sW1 + (k >> 2) * (kH * 128) + hh * (kHalf * 128) + (k & 3) * 32);
-          mma_bf16(d, da, db, kIdesc, k > 0 ? 1u : 0u);
+          mma_bf16_ts(d, tmem + kA1Col + buf * 64 + 8 * k, db, kIdesc, k > 0 ? 1u : 0u);
         }
       };
-      auto g2 = [&](int hh, int b) {  // D2[b] (+)= A2x * W2[:, x]^T, K = 128
-        const uint32_t d = tmem + 2 * kHalf + b * kC;
+      auto g2 = [&](int hh) {  // D2 (+)= A2x(tmem) * W2[:, x]^T, K = 128
+        const uint32_t d = tmem + kD2Col;
 #pragma unroll
         for (int k = 0; k < kHalf / 16; ++k) {
-          const uint64_t da = desc_sw128(sA2[hh] + (k >> 2) * (kTileRows * 128) + (k & 3) * 32);
           const uint64_t db =
               desc_sw128(sW2 + (hh * 2 + (k >> 2)) * (kC * 128) + (k & 3) * 32);
-          mma_bf16(d, da, db, kIdesc, (hh > 0 || k > 0) ? 1u : 0u);
+          mma_bf16_ts(d, tmem + hh * kHalf + a2_col(k), db, kIdesc, (hh > 0 || k > 0) ? 1u : 0u);
         }
       };
-      bool ok = mbar_wait_abortable(&bars[A1_FULL], 0, abort_flag);
+      bool ok = mbar_wait_abortable(&bars[A1_FULL0], 0, abort_flag);
       if (ok) {
         tc_fence_after();
-        g1(0);
+        g1(0, 0);
         mma_commit(&bars[D1A_FULL]);
-        g1(1);
+        g1(1, 0);
         mma_commit(&bars[D1B_FULL]);
-        mma_commit(&bars[A1_EMPTY]);
+        mma_commit(&bars[A1_EMPTY0]);
       }
       for (int it = 0; ok && it < n_my; ++it) {
-        const int b = it & 1;
         const bool next = it + 1 < n_my;
-        ok = mbar_wait_abortable(&bars[A2A_FULL], it & 1, abort_flag) &&
-             mbar_wait_abortable(&bars[D2_EMPTY0 + b], ((it >> 1) & 1) ^ 1, abort_flag);
+        const int nbuf = (it + 1) & 1;
+        ok = mbar_wait_abortable(&bars[A2A_FULL], it & 1, abort_flag);
         if (!ok) break;
         tc_fence_after();
-        g2(0, b);
-        mma_commit(&bars[A2A_EMPTY]);
-        if (next) {
-          ok = mbar_wait_abortable(&bars[A1_FULL], (it + 1) & 1, abort_flag);
-          if (!ok) break;
-          tc_fence_after();
-          g1(0);
-          mma_commit(&bars[D1A_FULL]);
+        g2(0);
+        // G2b(t) and G1a(t+1), whichever is ready first
+        bool g2b_done = false, g1a_done = !next;
+        const uint32_t a2b = smem_u32(&bars[A2B_FULL]);
+        const uint32_t a1f = smem_u32(&bars[A1_FULL0 + nbuf]);
+        const uint64_t t0 = global_ns();
+        for (uint32_t spin = 0; !(g2b_done && g1a_done); ++spin) {
+          if (!g2b_done && mbar_try(a2b, it & 1)) {
+            tc_fence_after();
+            g2(1);
+            mma_commit(&bars[D2_FULL]);
+            g2b_done = true;
+            continue;
+          }
+          if (!g1a_done && mbar_try(a1f, ((it + 1) >> 1) & 1)) {
+            tc_fence_after();
+            g1(0, nbuf);
+            mma_commit(&bars[D1A_FULL]);
+            g1a_done = true;
+            continue;
+          }
+          if ((spin & 255u) == 255u && (*abort_flag || global_ns() - t0 > kWaitNs)) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
         }
-        ok = mbar_wait_abortable(&bars[A2B_FULL], it & 1, abort_flag);
         if (!ok) break;
-        tc_fence_after();
-        g2(1, b);
-        mma_commit(&bars[A2B_EMPTY]);
-        mma_commit(&bars[D2_FULL0 + b]);
         if (next) {
-          g1(1);
+          g1(1, nbuf);
           mma_commit(&bars[D1B_FULL]);
-          mma_commit(&bars[A1_EMPTY]);
+          mma_commit(&bars[A1_EMPTY0 + nbuf]);
         }
       }
     }
@@ -1093,6 +1334,242 @@ __global__ void __launch_bounds__(256) count_head_kernel(
       logcounts[(long long)b * n_groups + g] = t;
     }
     __syncthreads();
+  }
+}
+
+// ============================================================== heads, tcgen05
+// Profile head as a GEMM plus a diagonal reduction (upstream
+// cherimoya.py:182-184, 379-384):
+//   Z[w, t] = sum_c Xc[p0 + w, c] * F[o, c, t]        (tcgen05, fp32 in TMEM)
+//   P[o, j] = bias[o] + sum_{t < 75} Z[j + t, t]       (fixed-order sums)
+// over the window w in [0, Lout + 74) starting at sequence position
+// p0 = T - 37, for one (output channel o, example b) per CTA. F is packed
+// transposed (taps x channels, K-major) as bf16 hi + lo parts, so X * F is
+// carried to ~16 bits; in fp32 mode X is split the same way (3 MMAs). The
+// count head is fused: the example's o == 0 CTA accumulates per-channel
+// sums of the rows in [T, L - T) while it stages them (fixed order), then
+// logcount[g] = bias[g] + sum_c Wl[g, c] mean[c] (+ Wl[g, C] log(1 + sum ctl)).
+namespace hd {
+constexpr int kNP = 80;            // 75 taps padded to an MMA N
+constexpr int kZStride = 77;       // Z ring row stride (floats): conflict-free diagonals
+constexpr int kRing = 208;         // ring rows: one tile + the 74-row halo, rounded up
+constexpr int kThreads = 128;
+}  // namespace hd
+
+struct HeadArgs {
+  int* status;            // set on a timed-out wait
+  const void* X;          // (B * L, CP) act_t
+  const float* X_ctl;     // (B, n_ctl, L) or null
+  const uint8_t* fb;      // packed F: per output o, [hi | lo] each kNP x CPH bf16 swizzled
+  const float* fbias;     // (n_out)
+  const float* lw;        // (n_groups, C (+1))
+  const float* lbias;     // (n_groups)
+  float* profile;         // (B, n_out, Lout)
+  float* logcounts;       // (B, n_groups)
+  int L, C, CP, CPH, n_ctl, n_out, n_groups, T, Lout;
+};
+
+__host__ __device__ constexpr uint32_t head_smem_bytes(int CPH, int a_splits) {
+  return static_cast<uint32_t>(2 * hd::kNP * CPH * 2 + a_splits * kTileRows * CPH * 2 +
+                               hd::kRing * hd::kZStride * 4 + 2048 + 64 + 1024);
+}
+
+template <typename act_t, int kASplits>
+__global__ void __launch_bounds__(hd::kThreads) head_kernel(HeadArgs a) {
+  using namespace hd;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int CPH = a.CPH;
+  uint8_t* sB = smem;                                          // [2][kNP x CPH]
+  uint8_t* sA = sB + 2 * kNP * CPH * 2;                        // [kASplits][128 x CPH]
+  float* ring = reinterpret_cast<float*>(sA + kASplits * kTileRows * CPH * 2);
+  float* red = ring + kRing * kZStride;                        // 512 floats
+  uint64_t* bar = reinterpret_cast<uint64_t*>(red + 512);
+  uint32_t* slot = reinterpret_cast<uint32_t*>(bar + 1);
+  const int o = blockIdx.x, b = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bool counts = (o == 0);
+
+  if (warp == 0) tmem_alloc(slot, 128);
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    mbar_init_fence();
+  }
+  {  // this output's packed F (hi and lo)
+    const uint4* g = reinterpret_cast<const uint4*>(a.fb + (size_t)o * 2 * kNP * CPH * 2);
+    uint4* d = reinterpret_cast<uint4*>(sB);
+    for (int i = tid; i < 2 * kNP * CPH * 2 / 16; i += blockDim.x) d[i] = g[i];
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *slot;
+  const int W = a.Lout + kHeadTaps - 1;
+  const int n_tiles = (W + kTileRows - 1) / kTileRows;
+  const int p0 = a.T - kHeadPad;
+  const int chunks = CPH / 8;                   // 16-byte channel chunks per row
+  const int my_chunk = tid % chunks;
+  const int row_step = kHeadThreadsRows(chunks);
+  float csum[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) csum[e] = 0.f;
+  float ctl_sum = 0.f;
+  const act_t* Xb = static_cast<const act_t*>(a.X) + (long long)b * a.L * a.CP;
+  const uint32_t sA_addr = smem_u32(sA), sB_addr = smem_u32(sB);
+  const uint32_t idesc = idesc_bf16(kTileRows, kNP);
+  bool ok = true;
+
+  for (int k = 0; k < n_tiles; ++k) {
+    // ---- stage window rows [128k, 128k + 128) as bf16 (hi [, lo]) operand tiles
+    for (int rr = tid / chunks; rr < kTileRows; rr += row_step) {
+      const int w = k * kTileRows + rr;
+      const int p = p0 + w;
+      const int c = my_chunk * 8;
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = 0.f;
+      if (w < W && p >= 0 && p < a.L) {
+        if (c + 8 <= a.C) {
+          load8(Xb + (long long)p * a.CP + c, v);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int ce = c + e;
+            if (ce < a.C) v[e] = to_f32<act_t>(Xb[(long long)p * a.CP + ce]);
+            else if (ce < a.C + a.n_ctl)
+              v[e] = a.X_ctl[((long long)b * a.n_ctl + (ce - a.C)) * a.L + p];
+          }
+        }
+        if (counts && p >= a.T && p < a.L - a.T) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            if (c + e < a.C) csum[e] += v[e];
+            else if (c + e < a.C + a.n_ctl) ctl_sum += v[e];
+          }
+        }
+      }
+      uint32_t hi[4], lo[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        hi[e] = pack_bf16x2(v[2 * e], v[2 * e + 1]);
+        if (kASplits > 1) {
+          const float h0 = __uint_as_float(hi[e] << 16), h1 = __uint_as_float(hi[e] & 0xFFFF0000u);
+          lo[e] = pack_bf16x2(v[2 * e] - h0, v[2 * e + 1] - h1);
+        }
+      }
+      const uint32_t off = sw128_offset(rr, c, kTileRows);
+      *reinterpret_cast<uint4*>(sA + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      if (kASplits > 1)
+        *reinterpret_cast<uint4*>(sA + kTileRows * CPH * 2 + off) =
+            make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    // ---- Z = A_hi F_hi + A_hi F_lo (+ A_lo F_hi)
+    if (tid == 0) {
+      tc_fence_after();
+      const int ksteps = CPH / 16;
+      uint32_t acc = 0;
+      for (int term = 0; term < (kASplits > 1 ? 3 : 2); ++term) {
+        const int ai = (term == 2) ? 1 : 0;
+        const int bi = (term == 1) ? 1 : 0;
+        for (int kk = 0; kk < ksteps; ++kk) {
+          const uint64_t da = desc_sw128(sA_addr + ai * (kTileRows * CPH * 2) +
+                                         (kk >> 2) * (kTileRows * 128) + (kk & 3) * 32);
+          const uint64_t db = desc_sw128(sB_addr + bi * (kNP * CPH * 2) +
+                                         (kk >> 2) * (kNP * 128) + (kk & 3) * 32);
+          mma_bf16(tmem, da, db, idesc, acc);
+          acc = 1;
+        }
+      }
+      mma_commit(bar);
+    }
+    ok = mbar_wait(bar, k & 1);
+    if (__syncthreads_or(!ok)) {
+      if (tid == 0) atomicExch(a.status, kStatusTimeout);
+      break;
+    }
+    tc_fence_after();
+    // ---- Z tile -> ring rows (128k + row) mod kRing (columns 0..74)
+    {
+      const int rr = warp * 32 + lane;
+      float* zrow = ring + ((k * kTileRows + rr) % kRing) * kZStride;
+      const uint32_t lane_sel = static_cast<uint32_t>(warp * 32) << 16;
+#pragma unroll 1
+      for (int part = 0; part < 3; ++part) {
+        const int col = part == 0 ? 0 : (part == 1 ? 32 : 48);   // 48..79 overlaps 32..63
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_sel + col, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int q = 0; q < 32; ++q) {
+          const int t = col + q;
+          if ((part < 2 || t >= 64) && t < kHeadTaps) zrow[t] = __uint_as_float(r[q]);
+        }
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+    // ---- outputs whose 75 rows are now all in the ring
+    // rows j .. j + 74 of output j lie in tiles <= k and the ring still holds
+    // rows >= 128k - 80
+    const int j_lo = (k == 0) ? 0 : k * kTileRows - (kHeadTaps - 1);
+    const int j_hi = (k == n_tiles - 1) ? a.Lout
+                                        : min(a.Lout, k * kTileRows + kTileRows - (kHeadTaps - 1));
+    for (int j = j_lo + tid; j < j_hi; j += blockDim.x) {
+      float acc = 0.f;
+      int rrow = j % kRing;
+#pragma unroll 5
+      for (int t = 0; t < kHeadTaps; ++t) {
+        acc += ring[rrow * kZStride + t];
+        rrow = (rrow + 1 == kRing) ? 0 : rrow + 1;
+      }
+      a.profile[((long long)b * a.n_out + o) * a.Lout + j] = acc + a.fbias[o];
+    }
+    __syncthreads();
+  }
+  if (counts) {
+    // fixed-order reduction of the per-thread channel sums
+    for (int e = 0; e < 8; ++e) {
+      red[tid] = csum[e];
+      __syncthreads();
+      if (tid < chunks) {
+        const int c = tid * 8 + e;
+        float s = 0.f;
+        for (int i = tid; i < blockDim.x; i += chunks) s += red[i];
+        if (c < a.C) red[256 + c] = s / static_cast<float>(a.Lout);
+      }
+      __syncthreads();
+    }
+    red[tid] = ctl_sum;
+    __syncthreads();
+    if (tid == 0) {
+      float cs = 0.f;
+      for (int i = 0; i < blockDim.x; ++i) cs += red[i];
+      red[255] = logf(cs + 1.0f);
+    }
+    __syncthreads();
+    const int cin = a.C + (a.n_ctl > 0 ? 1 : 0);
+    for (int g = warp; g < a.n_groups; g += blockDim.x / 32) {
+      float v = 0.f;
+      for (int c = lane; c < a.C; c += 32) v += a.lw[(long long)g * cin + c] * red[256 + c];
+#pragma unroll
+      for (int sh = 16; sh > 0; sh >>= 1) v += __shfl_xor_sync(0xffffffffu, v, sh);
+      if (lane == 0) {
+        float t = a.lbias[g] + v;
+        if (a.n_ctl > 0) t += a.lw[(long long)g * cin + a.C] * red[255];
+        a.logcounts[(long long)b * a.n_groups + g] = t;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 128);
   }
 }
 
@@ -1254,6 +1731,39 @@ __global__ void pack_sw128_kernel(const float* __restrict__ src, int R, int K, i
   const int r = i / KP, k = i - (i / KP) * KP;
   const float v = (r < R && k < K) ? src[(long long)r * K + k] * scale : 0.f;
   *reinterpret_cast<__nv_bfloat16*>(dst + sw128_offset(r, k, RP)) = __float2bfloat16_rn(v);
+}
+
+// hi / lo split of an fp32 (R, K) matrix into two bf16 swizzled tiles
+// (lo = value - bf16(value)); dst holds [hi | lo], each RP x KP.
+__global__ void pack_sw128_split_kernel(const float* __restrict__ src, int R, int K, int RP,
+                                        int KP, uint8_t* __restrict__ dst) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= RP * KP) return;
+  const int r = i / KP, k = i - (i / KP) * KP;
+  const float v = (r < R && k < K) ? src[(long long)r * K + k] : 0.f;
+  const __nv_bfloat16 h = __float2bfloat16_rn(v);
+  const uint32_t off = sw128_offset(r, k, RP);
+  *reinterpret_cast<__nv_bfloat16*>(dst + off) = h;
+  *reinterpret_cast<__nv_bfloat16*>(dst + (size_t)RP * KP * 2 + off) =
+      __float2bfloat16_rn(v - __bfloat162float(h));
+}
+
+// Profile-head weight F (n_out, Cin, 75) -> per output o a transposed
+// [taps x channels] operand, hi and lo: dst[o] = [hi | lo], each NP x CPH.
+__global__ void pack_head_kernel(const float* __restrict__ F, int n_out, int Cin, int taps,
+                                 int NP, int CPH, uint8_t* __restrict__ dst) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)n_out * NP * CPH) return;
+  const int o = static_cast<int>(i / ((long long)NP * CPH));
+  const int rem = static_cast<int>(i - (long long)o * NP * CPH);
+  const int t = rem / CPH, c = rem - (rem / CPH) * CPH;
+  const float v = (t < taps && c < Cin) ? F[((long long)o * Cin + c) * taps + t] : 0.f;
+  const __nv_bfloat16 h = __float2bfloat16_rn(v);
+  uint8_t* base = dst + (size_t)o * 2 * NP * CPH * 2;
+  const uint32_t off = sw128_offset(t, c, NP);
+  *reinterpret_cast<__nv_bfloat16*>(base + off) = h;
+  *reinterpret_cast<__nv_bfloat16*>(base + (size_t)NP * CPH * 2 + off) =
+      __float2bfloat16_rn(v - __bfloat162float(h));
 }
 
 // fp32 (3, C) -> (3, CP) zero padded.

@@ -139,6 +139,27 @@ def test_deterministic_and_batch_invariant(golden, mode):
     assert torch.equal(p3, p1[2:3]) and torch.equal(c3, c1[2:3])
 
 
+@pytest.mark.parametrize("mode", ["fp32", "bf16"])
+@pytest.mark.parametrize("dil", [1, 64, 256])
+def test_block_repeatable_over_many_tiles(mode, dil):
+    """Several 128-row tiles per CTA (64 x 2114 rows = 1057 tiles): the
+    pipelined kernel's buffer reuse is exercised; repeated calls must be
+    bitwise equal and match the oracle."""
+    torch.manual_seed(dil)
+    blk = cb.CheriBlock(128, dil).eval()
+    sd = {k: v.clone() for k, v in blk.state_dict().items()}
+    x = torch.randn(64, 2114, 128) * 0.3
+    ref = O.cheri_block(x, sd["conv_weight"], sd["linear1.weight"], sd["linear2.weight"], dil,
+                        0.15)
+    blk = blk.to(DEV)
+    dt = torch.float32 if mode == "fp32" else torch.bfloat16
+    with torch.no_grad():
+        outs = [blk(x.to(DEV, dt)).float().cpu() for _ in range(3)]
+    assert all(torch.equal(outs[0], o) for o in outs[1:])
+    err = (outs[0] - ref).abs().max().item()
+    assert err <= (FP32_TOL if mode == "fp32" else 3e-2), err
+
+
 @pytest.mark.parametrize("idx", [0, 1, 2])
 def test_block_engine_matches_upstream(golden, idx):
     c = golden("cheri_block")["cases"][idx]
