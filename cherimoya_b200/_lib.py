@@ -23,7 +23,7 @@ EXPORTED = (
     "chm_pack_weights", "chm_forward_workspace_bytes", "chm_forward", "chm_forward_bases",
     "chm_ism_workspace_bytes", "chm_ism", "chm_variant_workspace_bytes", "chm_variant",
     "chm_block_packed_bytes", "chm_pack_block", "chm_block_workspace_bytes",
-    "chm_block_forward", "chm_read_status", "chm_last_launch_count", "chm_timing_enable",
+    "chm_block_forward", "chm_forward_noalloc", "chm_read_status", "chm_last_launch_count", "chm_timing_enable",
     "chm_timing_collect",
 )
 TIMING_CLASSES = ("stem", "stats", "mlp", "profile_head", "count_head", "score", "other")
@@ -87,6 +87,7 @@ def _declare(lib):
         "chm_pack_block": (i32, [i32, i32, ctypes.c_float, vp, vp, vp, vp, sz, vp]),
         "chm_block_workspace_bytes": (sz, [i32, i32, i32, i32]),
         "chm_block_forward": (i32, [i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, sz, vp]),
+        "chm_forward_noalloc": (i32, [desc_p, vp, i32, vp, i32, vp, vp, vp, vp]),
         "chm_read_status": (i32, [vp, vp]),
         "chm_last_launch_count": (ctypes.c_int64, []),
         "chm_timing_enable": (None, [i32]),

@@ -543,6 +543,30 @@ int run_block_t(const Dims& m, int batch, int dil, const uint8_t* packed, const 
   return CHM_OK;
 }
 
+// ---- static scratch of chm_forward_noalloc (see the header): device code
+// could name the array directly; host code needs its device address, looked
+// up once per device with that device current.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[CHM_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+void* g_noalloc_base[kMaxDevices] = {};
+
+int noalloc_scratch(uint8_t** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CHM_ERR_CUDA;
+  if (dev < 0 || dev >= kMaxDevices) return CHM_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_base[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return CHM_ERR_CUDA;
+    g_noalloc_base[dev] = p;
+  }
+  // the forward wants a 1024-byte-aligned workspace
+  *out = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(g_noalloc_base[dev])));
+  return CHM_OK;
+}
+
 }  // namespace
 
 // ====================================================================== ABI
@@ -658,6 +682,26 @@ int32_t chm_forward(const chm_model_desc* desc, const void* packed, int32_t batc
   in.x_bf16 = (input_dtype == CHM_INPUT_BF16);
   return forward_common(desc, packed, batch, kInDense, in, x_ctl, profile, logcounts, workspace,
                         workspace_bytes, stream);
+}
+
+int32_t chm_forward_noalloc(const chm_model_desc* desc, const void* packed, int32_t batch,
+                            const void* x, int32_t input_dtype, const float* x_ctl,
+                            float* profile, float* logcounts, chm_stream_t stream) {
+  CHM_TRY(validate(desc));
+  if (batch < 0) return CHM_ERR_INVALID_ARGUMENT;
+  const size_t usable = CHM_NOALLOC_SCRATCH_BYTES - kAlign;   // after aligning the base
+  const size_t need = batch > 0 ? fwd_layout(dims_of(desc), batch).total : 0;
+  if (need > usable) {
+    fprintf(stderr,
+            "cherimoya_b200: chm_forward_noalloc: a batch of %d needs %zu bytes of scratch; "
+            "the static scratch holds %zu (split the batch)\n",
+            batch, need, usable);
+    return CHM_ERR_WORKSPACE;
+  }
+  uint8_t* ws = nullptr;
+  CHM_TRY(noalloc_scratch(&ws));
+  return chm_forward(desc, packed, batch, x, input_dtype, x_ctl, profile, logcounts, ws, usable,
+                     stream);
 }
 
 int32_t chm_forward_bases(const chm_model_desc* desc, const void* packed, int32_t batch,

@@ -180,6 +180,26 @@ int32_t chm_block_forward(int32_t batch, int32_t seq_len, int32_t n_filters, int
                           void* out, void* workspace, size_t workspace_bytes,
                           chm_stream_t stream);
 
+/* ---- forward without any device allocation ----
+ * No counterpart in the upstream project. For callers that cannot allocate
+ * device memory: a plugin host that owns every device buffer and lends only
+ * inputs and outputs, a foreign-language binding with no access to a device
+ * allocator, or code that must not call cudaMalloc (which can synchronise
+ * the device). Same computation and arguments as chm_forward minus the
+ * workspace: the scratch lives in a static device array of
+ * CHM_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until
+ * process exit. A batch whose scratch needs more than that is rejected with
+ * CHM_ERR_WORKSPACE (the default model at 2114 bp fits about 30 sequences per
+ * call in bf16 mode, 15 in fp32 mode). The first call on a device looks up
+ * the array's device address (cudaGetSymbolAddress) with that device
+ * current; make that first call before any stream capture. All calls share
+ * the one array, so calls that overlap on the GPU (different streams, or
+ * different host threads) race: order them. */
+#define CHM_NOALLOC_SCRATCH_BYTES (32u << 20)
+int32_t chm_forward_noalloc(const chm_model_desc* desc, const void* packed, int32_t batch,
+                            const void* x, int32_t input_dtype, const float* x_ctl,
+                            float* profile, float* logcounts, chm_stream_t stream);
+
 /* Synchronises `stream`, returns and clears the device status word that
  * the kernels of the last calls recorded in `workspace`. */
 int32_t chm_read_status(void* workspace, chm_stream_t stream);
