@@ -187,20 +187,23 @@ EncodeTiledFn encode_tiled() {
   return fn;
 }
 
-// Activation matrix (rows, CP) as a 2-D tensor of 128-byte x 128-row boxes
-// with the 128-byte swizzle; out-of-range rows read as zero.
-int make_act_tmap(CUtensorMap* map, const void* base, long long rows, int CP, int elem_bytes) {
+// Activation matrix (rows, CP) as a 2-D tensor of box_bytes x 128-row boxes
+// with the matching swizzle (64 or 128 bytes); out-of-range rows read as
+// zero and are not written by stores.
+int make_act_tmap(CUtensorMap* map, const void* base, long long rows, int CP, int elem_bytes,
+                  int box_bytes) {
   EncodeTiledFn fn = encode_tiled();
   if (!fn) return CHM_ERR_CUDA;
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return CHM_ERR_WORKSPACE;
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(CP), static_cast<cuuint64_t>(rows)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(CP) * elem_bytes};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / elem_bytes), 128u};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_bytes / elem_bytes), 128u};
   const cuuint32_t estr[2] = {1u, 1u};
   const CUresult r = fn(map, elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
                         2, const_cast<void*>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        box_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? CHM_OK : CHM_ERR_CUDA;
 }
@@ -227,8 +230,10 @@ int launch_mlp(const Dims& m, const MlpArgs& a, int grid, cudaStream_t st) {
   const bool fast = (m.mode == CHM_MODE_BF16);
   if (m.CP == ws::kC && m.HP == ws::kH) {
     const int smem = ws::kAlloc;
-    CUtensorMap tmap;
-    CHM_TRY(make_act_tmap(&tmap, a.X_in, a.rows, m.CP, sizeof(act_t)));
+    MlpMaps tmap;
+    CHM_TRY(make_act_tmap(&tmap.stage, a.X_in, a.rows, m.CP, sizeof(act_t), ws::kBoxBytes));
+    CHM_TRY(make_act_tmap(&tmap.res, a.X_in, a.rows, m.CP, sizeof(act_t), 128));
+    CHM_TRY(make_act_tmap(&tmap.out, a.X_out, a.rows, m.CP, sizeof(act_t), 128));
     LaunchTimer timer(kKMlp, st);
     if (fast) {
       auto k = mlp_ws_kernel<act_t, true>;

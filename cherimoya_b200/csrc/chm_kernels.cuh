@@ -841,9 +841,10 @@ __global__ void __launch_bounds__(128, 1) mlp_kernel(MlpArgs a) {
 // Warp-specialised persistent version of mlp_kernel for the default width
 // (C = 128, H = 256). Roles, per CTA (one CTA per SM):
 //   warps 0-3   producer : TMA loads of the three row blocks a tile's conv
-//                          reads (rows - d, rows, rows + d) into a swizzled
-//                          staging buffer; conv + LayerNorm (thread = row);
-//                          bf16 result written into TMEM (A operand of GEMM1)
+//                          reads (rows - d, rows, rows + d), 64-byte channel
+//                          boxes into a 2-slot staging ring; conv + LayerNorm
+//                          (thread = row); bf16 result written into TMEM
+//                          (A operand of GEMM1)
 //   warps 4-11  epilogue : GELU of the D1 halves, written back into TMEM as
 //                          bf16 (A operand of GEMM2); residual of D2
 //   warp 12     MMA      : one elected thread issues all tcgen05.mma
@@ -856,25 +857,30 @@ __global__ void __launch_bounds__(128, 1) mlp_kernel(MlpArgs a) {
 // A1[0] [384,448) | A1[1] [448,512). The bf16 GELU output of half x lives in
 // D1x's own columns: epilogue warpgroup g packs h [64g, 64g+64) of the half
 // into columns [64g, 64g+32), which it has already read.
-// Shared memory: W1 64 KB + W2 64 KB (resident), staging 2 slots x 48 KB
-// (each: the three row blocks of one 128-byte channel box, 128 rows each),
-// conv weights. A tile is processed box by box (2 boxes of 64 bf16 channels,
-// or 4 of 32 fp32 channels); the TMA for box step k + 2 is issued as soon as
-// box step k has been consumed, so loads overlap the conv of the next box.
+// Residual (bf16 mode): the tile's input rows arrive by TMA in a 128-byte
+// swizzled buffer, the epilogue adds D2 in place, and a TMA tile store
+// writes the result: every global access of the tile is a bulk transfer.
+// (fp32 mode adds D2 to rows read directly from global memory.)
+// Shared memory: W1 64 KB + W2 64 KB (resident), staging 2 slots x 24 KB
+// (three row blocks of one 64-byte channel box, 128 rows each), residual
+// tile 32 KB, conv weights.
 namespace ws {
 constexpr int kC = 128, kH = 256, kHalf = 128;
 constexpr int kProducerWarps = 4, kEpilogueWarps = 8;
 constexpr int kMmaWarp = kProducerWarps + kEpilogueWarps;      // 12
 constexpr int kThreads = (kMmaWarp + 1) * 32;                   // 416
-constexpr uint32_t kBox = 128 * 128;                            // 16 KB TMA box
+constexpr uint32_t kBoxBytes = 64;                              // staging box row width
+constexpr uint32_t kBox = kBoxBytes * 128;                      // 8 KB staging box
+constexpr uint32_t kResBox = 128 * 128;                         // 16 KB residual box
 constexpr uint32_t kW1 = 0;                                     // 256 x 128 bf16
 constexpr uint32_t kW2 = kW1 + kH * kC * 2;                     // 128 x 256 bf16
 constexpr uint32_t kStg = kW2 + kC * kH * 2;                    // 2 slots x 3 boxes
 constexpr uint32_t kSlotBytes = 3 * kBox;
-constexpr uint32_t kConvW = kStg + 2 * kSlotBytes;              // 3 x 128 fp32
+constexpr uint32_t kRes = kStg + 2 * kSlotBytes;                // 2 boxes (bf16 tile)
+constexpr uint32_t kConvW = kRes + 2 * kResBox;                 // 3 x 128 fp32
 constexpr uint32_t kBars = kConvW + 3 * kC * 4;
 enum Bar { STG_FULL0, STG_FULL1, STG_EMPTY0, STG_EMPTY1, A1_FULL0, A1_FULL1, A1_EMPTY0,
-           A1_EMPTY1, D1A_FULL, D1B_FULL, A2A_FULL, A2B_FULL, D2_FULL, kNumBars };
+           A1_EMPTY1, D1A_FULL, D1B_FULL, A2A_FULL, A2B_FULL, D2_FULL, RES_FULL, kNumBars };
 constexpr uint32_t kSlot = kBars + kNumBars * 8;
 constexpr uint32_t kAbort = kSlot + 4;
 constexpr uint32_t kBytes = kAbort + 4;
@@ -884,9 +890,15 @@ constexpr uint32_t kD2Col = 256, kA1Col = 384;
 __host__ __device__ constexpr uint32_t a2_col(int s) { return s < 4 ? 8 * s : 64 + 8 * (s - 4); }
 }  // namespace ws
 
+struct MlpMaps {
+  CUtensorMap stage;   // X_in, 64-byte x 128-row boxes, 64-byte swizzle
+  CUtensorMap res;     // X_in, 128-byte x 128-row boxes, 128-byte swizzle (bf16 residual)
+  CUtensorMap out;     // X_out, same boxes as `res`
+};
+
 template <typename act_t, bool kFastGelu>
 __global__ void __launch_bounds__(ws::kThreads, 1)
-    mlp_ws_kernel(MlpArgs a, const __grid_constant__ CUtensorMap tmap_x) {
+    mlp_ws_kernel(MlpArgs a, const __grid_constant__ MlpMaps maps) {
   using namespace ws;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -898,14 +910,15 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const act_t* Xi = static_cast<const act_t*>(a.X_in);
   act_t* Xo = static_cast<act_t*>(a.X_out);
-  constexpr int kBoxCh = 128 / sizeof(act_t);                   // channels per TMA box
+  constexpr bool kTmaResidual = sizeof(act_t) == 2;
+  constexpr int kBoxCh = kBoxBytes / sizeof(act_t);             // channels per staging box
   constexpr int kBoxes = kC / kBoxCh;                           // box steps per tile
 
   if (warp == kMmaWarp) tmem_alloc(slot, 512);
   if (tid == 0) {
     const uint32_t counts[kNumBars] = {1, 1, kProducerWarps * 32, kProducerWarps * 32,
                                        kProducerWarps * 32, kProducerWarps * 32, 1, 1, 1, 1,
-                                       kEpilogueWarps * 32, kEpilogueWarps * 32, 1};
+                                       kEpilogueWarps * 32, kEpilogueWarps * 32, 1, 1};
     for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], counts[i]);
     *abort_flag = 0;
     mbar_init_fence();
@@ -947,13 +960,14 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       mbar_expect_tx(&bars[STG_FULL0 + slotk], kSlotBytes);
 #pragma unroll
       for (int blk = 0; blk < 3; ++blk)
-        tma_load_2d(smem + kStg + (slotk * 3 + blk) * kBox, &tmap_x, b * kBoxCh,
+        tma_load_2d(smem + kStg + (slotk * 3 + blk) * kBox, &maps.stage, b * kBoxCh,
                     y0 + (blk - 1) * a.dil, &bars[STG_FULL0 + slotk]);
     };
     if (tid == 0) {
       issue(0);
       issue(1);
     }
+    __syncwarp();
     uint32_t k = 0;
     bool ok = true;
     for (int it = 0; it < n_my && ok; ++it) {
@@ -980,15 +994,17 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
           if (!ok) break;
           tc_fence_after();
         }
-        // conv + LayerNorm of this thread's row over the box's channels
-        const uint8_t* bL = smem + kStg + (slotk * 3 + 0) * kBox + rl * 128;
+        // conv + LayerNorm of this thread's row over the box's channels; the
+        // box rows are 64 bytes with the 64-byte swizzle (16-byte chunk q of
+        // row r at chunk q ^ ((r >> 1) & 3))
+        const uint8_t* bL = smem + kStg + (slotk * 3 + 0) * kBox + rl * kBoxBytes;
         const uint8_t* bC = bL + kBox;
         const uint8_t* bR = bL + 2 * kBox;
         const int cbase = b * kBoxCh;              // first channel of the box
         uint32_t packed[kBoxCh / 2];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {              // 16-byte chunks of the row
-          const uint32_t off = static_cast<uint32_t>((q ^ (rl & 7)) * 16);
+        for (int q = 0; q < 4; ++q) {              // 16-byte chunks of the row
+          const uint32_t off = static_cast<uint32_t>((q ^ ((rl >> 1) & 3)) * 16);
           uint4 vl = *reinterpret_cast<const uint4*>(bL + off);
           const uint4 vc = *reinterpret_cast<const uint4*>(bC + off);
           uint4 vr = *reinterpret_cast<const uint4*>(bR + off);
@@ -1031,14 +1047,13 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
           ok = mbar_wait_abortable(&bars[STG_EMPTY0 + slotk], (k >> 1) & 1, abort_flag);
           if (ok) issue(k + 2);
         }
+        __syncwarp();
         // packed channels [cbase, cbase + kBoxCh) -> A1 columns cbase / 2 ...
         const uint32_t col = tmem + lane_sel + kA1Col + buf * 64 + cbase / 2;
-#pragma unroll
-        for (int h = 0; h < kBoxCh / 32; ++h) {
-          uint32_t pp[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) pp[e] = packed[h * 16 + e];
-          tmem_st16(col + h * 16, pp);
+        if constexpr (kBoxCh / 2 == 16) {
+          tmem_st16(col, packed);
+        } else {
+          tmem_st8(col, packed);
         }
         if (!ok) break;
       }
@@ -1054,6 +1069,17 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
     const int g = ew >> 2;                         // warpgroup: half columns [64g, 64g+64)
     const int rl = quarter * 32 + lane;            // tile row of this thread
     const uint32_t lane_sel = static_cast<uint32_t>(quarter * 32) << 16;
+    const bool leader = (ew == 0 && lane == 0);    // issues the residual TMA
+    uint8_t* sRes = smem + kRes;
+    if constexpr (kTmaResidual) {
+      if (leader && n_my > 0) {
+        mbar_expect_tx(&bars[RES_FULL], 2 * kResBox);
+        const int y0 = first * kTileRows;
+        tma_load_2d(sRes, &maps.res, 0, y0, &bars[RES_FULL]);
+        tma_load_2d(sRes + kResBox, &maps.res, 64, y0, &bars[RES_FULL]);
+      }
+      __syncwarp();
+    }
     for (int it = 0; it < n_my; ++it) {
       const long long row0 = (long long)(first + it * stride) * kTileRows;
       bool ok = true;
@@ -1068,7 +1094,6 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
         for (int j = 0; j < 2; ++j) {
           uint32_t r[32];
           tmem_ld32(base + j * 32, r);
-          tmem_ld_wait();
           uint32_t p[16];
 #pragma unroll
           for (int q = 0; q < 16; ++q) {
@@ -1086,44 +1111,78 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
         mbar_arrive(&bars[hh ? A2B_FULL : A2A_FULL]);
       }
       if (!ok) break;
-      // residual of D2; the thread's input channels are fetched before the
-      // wait (they do not depend on the MMAs)
       const long long r = row0 + rl;
       const bool rv = r < a.rows;
-      constexpr int kVE = 16 / sizeof(act_t);      // elements per 16-byte vector
-      constexpr int kPre = 32 / kVE;                // vectors of one 32-column chunk
-      // bf16: both 32-column chunks prefetched (8 vectors); fp32: the first
-      constexpr int kPreAll = sizeof(act_t) == 2 ? 2 * kPre : kPre;
-      const act_t* xrow = Xi + r * kC + g * 64;
-      act_t* orow = Xo + r * kC + g * 64;
-      uint4 xin[kPreAll];
+      if constexpr (kTmaResidual) {
+        // residual of D2 through the TMA-loaded input tile, in place
+        if (!mbar_wait_abortable(&bars[RES_FULL], it & 1, abort_flag)) break;
+        if (!mbar_wait_abortable(&bars[D2_FULL], it & 1, abort_flag)) break;
+        tc_fence_after();
+        uint8_t* rowp = sRes + g * kResBox + rl * 128;   // this thread's 64 channels
 #pragma unroll
-      for (int q = 0; q < kPreAll; ++q)
-        xin[q] = rv ? *reinterpret_cast<const uint4*>(xrow + q * kVE) : make_uint4(0, 0, 0, 0);
-      if (!mbar_wait_abortable(&bars[D2_FULL], it & 1, abort_flag)) break;
-      tc_fence_after();
-      const uint32_t tcol = tmem + kD2Col + g * 64;
+        for (int j = 0; j < 2; ++j) {
+          uint32_t d[32];
+          tmem_ld32(tmem + lane_sel + kD2Col + g * 64 + j * 32, d);
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        uint32_t d[32];
-        tmem_ld32(tcol + lane_sel + j * 32, d);
-        if (kPreAll == kPre && j == 1) {
-#pragma unroll
-          for (int q = 0; q < kPre; ++q)
-            xin[q % kPreAll] = rv ? *reinterpret_cast<const uint4*>(xrow + 32 + q * kVE)
-                                  : make_uint4(0, 0, 0, 0);
+          for (int q = 0; q < 4; ++q) {
+            const int chunk = j * 4 + q;                  // 8 channels per chunk
+            uint4* ptr = reinterpret_cast<uint4*>(rowp + ((chunk ^ (rl & 7)) * 16));
+            *ptr = add_residual<act_t>(*ptr, d + q * 8);
+          }
         }
-        tmem_ld_wait();
-        if (rv) {
-#pragma unroll
-          for (int q = 0; q < kPre; ++q)
-            *reinterpret_cast<uint4*>(orow + j * 32 + q * kVE) =
-                add_residual<act_t>(xin[(kPreAll == kPre) ? q : j * kPre + q], d + q * kVE);
+        tc_fence_before();
+        fence_async_smem();                               // generic writes -> TMA store
+        named_sync(1, kEpilogueWarps * 32);
+        if (leader) {
+          tma_store_2d(&maps.out, sRes, 0, static_cast<int>(row0));
+          tma_store_2d(&maps.out, sRes + kResBox, 64, static_cast<int>(row0));
+          bulk_commit();
+          if (it + 1 < n_my) {
+            bulk_wait_read0();                            // the tile buffer is free again
+            mbar_expect_tx(&bars[RES_FULL], 2 * kResBox);
+            const int y1 = (first + (it + 1) * stride) * kTileRows;
+            tma_load_2d(sRes, &maps.res, 0, y1, &bars[RES_FULL]);
+            tma_load_2d(sRes + kResBox, &maps.res, 64, y1, &bars[RES_FULL]);
+          }
         }
+        __syncwarp();
+      } else {
+        // residual of D2 on rows read directly from global memory (fp32)
+        constexpr int kVE = 16 / sizeof(act_t);
+        constexpr int kPre = 32 / kVE;
+        const act_t* xrow = Xi + r * kC + g * 64;
+        act_t* orow = Xo + r * kC + g * 64;
+        uint4 xin[kPre];
+#pragma unroll
+        for (int q = 0; q < kPre; ++q)
+          xin[q] = rv ? *reinterpret_cast<const uint4*>(xrow + q * kVE) : make_uint4(0, 0, 0, 0);
+        if (!mbar_wait_abortable(&bars[D2_FULL], it & 1, abort_flag)) break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int j = 0; j < 2; ++j) {
+          uint32_t d[32];
+          tmem_ld32(tmem + lane_sel + kD2Col + g * 64 + j * 32, d);
+          if (j == 1) {
+#pragma unroll
+            for (int q = 0; q < kPre; ++q)
+              xin[q] = rv ? *reinterpret_cast<const uint4*>(xrow + 32 + q * kVE)
+                          : make_uint4(0, 0, 0, 0);
+          }
+          if (rv) {
+#pragma unroll
+            for (int q = 0; q < kPre; ++q)
+              *reinterpret_cast<uint4*>(orow + j * 32 + q * kVE) =
+                  add_residual<act_t>(xin[q], d + q * kVE);
+          }
+        }
+        tc_fence_before();
       }
       // D2 is next written by G2a(t+1), which the MMA issues only after this
       // warpgroup's GELU of tile t+1: program order protects it.
-      tc_fence_before();
+    }
+    if constexpr (kTmaResidual) {
+      if (leader) bulk_wait0();                           // stores done before exit
+      __syncwarp();
     }
   } else {
     // ------------------------------------------------------------ MMA issuer
@@ -1133,19 +1192,20 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       auto g1 = [&](int hh, int buf) {  // D1x = A1(tmem) * W1[hh*128 : hh*128+128]^T, K = 128
         const uint32_t d = tmem + hh * kHalf;
 #pragma unroll
-        for (int k = 0; k < kC / 16; ++k) {
+        for (int kk = 0; kk < kC / 16; ++kk) {
           const uint64_t db =
-              desc_sw128(sW1 + (k >> 2) * (kH * 128) + hh * (kHalf * 128) + (k & 3) * 32);
-          mma_bf16_ts(d, tmem + kA1Col + buf * 64 + 8 * k, db, kIdesc, k > 0 ? 1u : 0u);
+              desc_sw128(sW1 + (kk >> 2) * (kH * 128) + hh * (kHalf * 128) + (kk & 3) * 32);
+          mma_bf16_ts(d, tmem + kA1Col + buf * 64 + 8 * kk, db, kIdesc, kk > 0 ? 1u : 0u);
         }
       };
       auto g2 = [&](int hh) {  // D2 (+)= A2x(tmem) * W2[:, x]^T, K = 128
         const uint32_t d = tmem + kD2Col;
 #pragma unroll
-        for (int k = 0; k < kHalf / 16; ++k) {
+        for (int kk = 0; kk < kHalf / 16; ++kk) {
           const uint64_t db =
-              desc_sw128(sW2 + (hh * 2 + (k >> 2)) * (kC * 128) + (k & 3) * 32);
-          mma_bf16_ts(d, tmem + hh * kHalf + a2_col(k), db, kIdesc, (hh > 0 || k > 0) ? 1u : 0u);
+              desc_sw128(sW2 + (hh * 2 + (kk >> 2)) * (kC * 128) + (kk & 3) * 32);
+          mma_bf16_ts(d, tmem + hh * kHalf + a2_col(kk), db, kIdesc,
+                      (hh > 0 || kk > 0) ? 1u : 0u);
         }
       };
       bool ok = mbar_wait_abortable(&bars[A1_FULL0], 0, abort_flag);
