@@ -848,6 +848,9 @@ __global__ void __launch_bounds__(128, 1) mlp_kernel(MlpArgs a) {
 //   warps 4-11  epilogue : GELU of the D1 halves, written back into TMEM as
 //                          bf16 (A operand of GEMM2); residual of D2
 //   warp 12     MMA      : one elected thread issues all tcgen05.mma
+//   warp 13     TMA      : one thread refills staging slots as they are
+//                          released, stores finished residual tiles and
+//                          loads the next tile's input rows
 // H is split in halves (a: h 0..127, b: h 128..255). G1x: D1x = A1 * W1[x]^T,
 // G2x: D2 (+)= gelu(D1x) * W2[:, x]^T; both take A from TMEM. MMAs issued by
 // one thread execute in order, so G1x(t+1) overwriting D1x cannot overtake
@@ -868,7 +871,8 @@ namespace ws {
 constexpr int kC = 128, kH = 256, kHalf = 128;
 constexpr int kProducerWarps = 4, kEpilogueWarps = 8;
 constexpr int kMmaWarp = kProducerWarps + kEpilogueWarps;      // 12
-constexpr int kThreads = (kMmaWarp + 1) * 32;                   // 416
+constexpr int kTmaWarp = kMmaWarp + 1;                          // 13
+constexpr int kThreads = (kTmaWarp + 1) * 32;                   // 448
 constexpr uint32_t kBoxBytes = 64;                              // staging box row width
 constexpr uint32_t kBox = kBoxBytes * 128;                      // 8 KB staging box
 constexpr uint32_t kResBox = 128 * 128;                         // 16 KB residual box
@@ -880,7 +884,8 @@ constexpr uint32_t kRes = kStg + 2 * kSlotBytes;                // 2 boxes (bf16
 constexpr uint32_t kConvW = kRes + 2 * kResBox;                 // 3 x 128 fp32
 constexpr uint32_t kBars = kConvW + 3 * kC * 4;
 enum Bar { STG_FULL0, STG_FULL1, STG_EMPTY0, STG_EMPTY1, A1_FULL0, A1_FULL1, A1_EMPTY0,
-           A1_EMPTY1, D1A_FULL, D1B_FULL, A2A_FULL, A2B_FULL, D2_FULL, RES_FULL, kNumBars };
+           A1_EMPTY1, D1A_FULL, D1B_FULL, A2A_FULL, A2B_FULL, D2_FULL, RES_FULL, RES_DONE,
+           kNumBars };
 constexpr uint32_t kSlot = kBars + kNumBars * 8;
 constexpr uint32_t kAbort = kSlot + 4;
 constexpr uint32_t kBytes = kAbort + 4;
@@ -918,7 +923,8 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
   if (tid == 0) {
     const uint32_t counts[kNumBars] = {1, 1, kProducerWarps * 32, kProducerWarps * 32,
                                        kProducerWarps * 32, kProducerWarps * 32, 1, 1, 1, 1,
-                                       kEpilogueWarps * 32, kEpilogueWarps * 32, 1, 1};
+                                       kEpilogueWarps * 32, kEpilogueWarps * 32, 1, 1,
+                                       kEpilogueWarps * 32};
     for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], counts[i]);
     *abort_flag = 0;
     mbar_init_fence();
@@ -950,24 +956,6 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
     const int quarter = warp & 3;                 // TMEM lane quarter = tile rows
     const int rl = quarter * 32 + lane;           // tile row of this thread
     const uint32_t lane_sel = static_cast<uint32_t>(quarter * 32) << 16;
-    // box step k -> (tile it = k / kBoxes, box b = k % kBoxes) into slot k & 1
-    auto issue = [&](uint32_t k) {
-      const int tit = static_cast<int>(k / kBoxes);
-      if (tit >= n_my) return;
-      const int b = static_cast<int>(k % kBoxes);
-      const int slotk = k & 1;
-      const int y0 = (first + tit * stride) * kTileRows;
-      mbar_expect_tx(&bars[STG_FULL0 + slotk], kSlotBytes);
-#pragma unroll
-      for (int blk = 0; blk < 3; ++blk)
-        tma_load_2d(smem + kStg + (slotk * 3 + blk) * kBox, &maps.stage, b * kBoxCh,
-                    y0 + (blk - 1) * a.dil, &bars[STG_FULL0 + slotk]);
-    };
-    if (tid == 0) {
-      issue(0);
-      issue(1);
-    }
-    __syncwarp();
     uint32_t k = 0;
     bool ok = true;
     for (int it = 0; it < n_my && ok; ++it) {
@@ -1037,17 +1025,12 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
 #pragma unroll
           for (int e = 0; e < kBoxCh / 2; ++e) packed[e] = 0u;
         }
-        // staging consumed: release the slot; thread 0 refills it (box k + 2).
-        // The proxy fence orders these generic-proxy reads before the TMA
-        // (async proxy) overwrites the slot; without it the refill can land
-        // before the reads complete.
+        // staging consumed: release the slot (the TMA warp refills it with
+        // box k + 2). The proxy fence orders these generic-proxy reads before
+        // the TMA (async proxy) overwrites the slot; without it the refill
+        // can land before the reads complete.
         fence_async_smem();
         mbar_arrive(&bars[STG_EMPTY0 + slotk]);
-        if (tid == 0) {
-          ok = mbar_wait_abortable(&bars[STG_EMPTY0 + slotk], (k >> 1) & 1, abort_flag);
-          if (ok) issue(k + 2);
-        }
-        __syncwarp();
         // packed channels [cbase, cbase + kBoxCh) -> A1 columns cbase / 2 ...
         const uint32_t col = tmem + lane_sel + kA1Col + buf * 64 + cbase / 2;
         if constexpr (kBoxCh / 2 == 16) {
@@ -1069,17 +1052,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
     const int g = ew >> 2;                         // warpgroup: half columns [64g, 64g+64)
     const int rl = quarter * 32 + lane;            // tile row of this thread
     const uint32_t lane_sel = static_cast<uint32_t>(quarter * 32) << 16;
-    const bool leader = (ew == 0 && lane == 0);    // issues the residual TMA
     uint8_t* sRes = smem + kRes;
-    if constexpr (kTmaResidual) {
-      if (leader && n_my > 0) {
-        mbar_expect_tx(&bars[RES_FULL], 2 * kResBox);
-        const int y0 = first * kTileRows;
-        tma_load_2d(sRes, &maps.res, 0, y0, &bars[RES_FULL]);
-        tma_load_2d(sRes + kResBox, &maps.res, 64, y0, &bars[RES_FULL]);
-      }
-      __syncwarp();
-    }
     for (int it = 0; it < n_my; ++it) {
       const long long row0 = (long long)(first + it * stride) * kTileRows;
       bool ok = true;
@@ -1132,20 +1105,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
         }
         tc_fence_before();
         fence_async_smem();                               // generic writes -> TMA store
-        named_sync(1, kEpilogueWarps * 32);
-        if (leader) {
-          tma_store_2d(&maps.out, sRes, 0, static_cast<int>(row0));
-          tma_store_2d(&maps.out, sRes + kResBox, 64, static_cast<int>(row0));
-          bulk_commit();
-          if (it + 1 < n_my) {
-            bulk_wait_read0();                            // the tile buffer is free again
-            mbar_expect_tx(&bars[RES_FULL], 2 * kResBox);
-            const int y1 = (first + (it + 1) * stride) * kTileRows;
-            tma_load_2d(sRes, &maps.res, 0, y1, &bars[RES_FULL]);
-            tma_load_2d(sRes + kResBox, &maps.res, 64, y1, &bars[RES_FULL]);
-          }
-        }
-        __syncwarp();
+        mbar_arrive(&bars[RES_DONE]);                     // the TMA warp stores the tile
       } else {
         // residual of D2 on rows read directly from global memory (fp32)
         constexpr int kVE = 16 / sizeof(act_t);
@@ -1180,11 +1140,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       // D2 is next written by G2a(t+1), which the MMA issues only after this
       // warpgroup's GELU of tile t+1: program order protects it.
     }
-    if constexpr (kTmaResidual) {
-      if (leader) bulk_wait0();                           // stores done before exit
-      __syncwarp();
-    }
-  } else {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && n_my > 0) {
       const uint32_t sW1 = smem_u32(smem + kW1), sW2 = smem_u32(smem + kW2);
@@ -1257,6 +1213,67 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
           mma_commit(&bars[A1_EMPTY0 + nbuf]);
         }
       }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ TMA warp
+    if (lane == 0 && n_my > 0) {
+      // staging box step k -> (tile k / kBoxes, box k % kBoxes) into slot k & 1
+      auto issue = [&](uint32_t k) {
+        const int tit = static_cast<int>(k / kBoxes);
+        const int b = static_cast<int>(k % kBoxes);
+        const int slotk = k & 1;
+        const int y0 = (first + tit * stride) * kTileRows;
+        mbar_expect_tx(&bars[STG_FULL0 + slotk], kSlotBytes);
+#pragma unroll
+        for (int blk = 0; blk < 3; ++blk)
+          tma_load_2d(smem + kStg + (slotk * 3 + blk) * kBox, &maps.stage, b * kBoxCh,
+                      y0 + (blk - 1) * a.dil, &bars[STG_FULL0 + slotk]);
+      };
+      auto load_res = [&](int tit) {
+        mbar_expect_tx(&bars[RES_FULL], 2 * kResBox);
+        const int y0 = (first + tit * stride) * kTileRows;
+        tma_load_2d(smem + kRes, &maps.res, 0, y0, &bars[RES_FULL]);
+        tma_load_2d(smem + kRes + kResBox, &maps.res, 64, y0, &bars[RES_FULL]);
+      };
+      const uint32_t n_steps = static_cast<uint32_t>(n_my) * kBoxes;
+      issue(0);
+      if (n_steps > 1) issue(1);
+      if (kTmaResidual) load_res(0);
+      uint32_t k_next = 2;                 // next staging box step to issue
+      int r_next = kTmaResidual ? 0 : n_my; // next residual tile to store
+      const uint64_t t0 = global_ns();
+      uint64_t last_progress = t0;
+      for (uint32_t spin = 0; k_next < n_steps || r_next < n_my; ++spin) {
+        bool progress = false;
+        if (k_next < n_steps &&
+            mbar_try(smem_u32(&bars[STG_EMPTY0 + (k_next & 1)]), ((k_next - 2) >> 1) & 1)) {
+          issue(k_next);
+          ++k_next;
+          progress = true;
+        }
+        if (r_next < n_my && mbar_try(smem_u32(&bars[RES_DONE]), r_next & 1)) {
+          const int y0 = (first + r_next * stride) * kTileRows;
+          tma_store_2d(&maps.out, smem + kRes, 0, y0);
+          tma_store_2d(&maps.out, smem + kRes + kResBox, 64, y0);
+          bulk_commit();
+          if (r_next + 1 < n_my) {
+            bulk_wait_read0();             // the tile buffer is free again
+            load_res(r_next + 1);
+          }
+          ++r_next;
+          progress = true;
+        }
+        if (progress) {
+          last_progress = global_ns();
+        } else if ((spin & 255u) == 255u) {
+          if (*abort_flag || global_ns() - last_progress > kWaitNs) {
+            *abort_flag = 1;
+            break;
+          }
+        }
+      }
+      bulk_wait0();                        // residual stores complete before exit
     }
     __syncwarp();
   }
