@@ -208,6 +208,26 @@ int make_act_tmap(CUtensorMap* map, const void* base, long long rows, int CP, in
   return r == CUDA_SUCCESS ? CHM_OK : CHM_ERR_CUDA;
 }
 
+// Activations as a 3-D tensor (channels, L, batch) of 128-byte x 128-row x 1
+// boxes with the 128-byte swizzle: rows outside [0, L) of an example read as
+// zero (the conv's zero padding).
+int make_act_tmap3(CUtensorMap* map, const void* base, int batch, int L, int CP) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn) return CHM_ERR_CUDA;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return CHM_ERR_WORKSPACE;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(CP), static_cast<cuuint64_t>(L),
+                              static_cast<cuuint64_t>(batch)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(CP) * 2,
+                                 static_cast<cuuint64_t>(CP) * 2 * L};
+  const cuuint32_t box[3] = {64u, 128u, 1u};
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? CHM_OK : CHM_ERR_CUDA;
+}
+
 // ---- MLP kernel dispatch over (act_t, CP, HP)
 template <typename act_t, int CP, int HP>
 int launch_mlp_t(const MlpArgs& a, int grid, cudaStream_t st, bool fast) {
@@ -265,9 +285,34 @@ int launch_mlp(const Dims& m, const MlpArgs& a, int grid, cudaStream_t st) {
 
 template <typename act_t>
 int launch_stats(const Dims& m, const act_t* X, const float* convw, int dil, int batch,
-                 float* partials, unsigned* counters, float2* stats, cudaStream_t st) {
+                 float* partials, unsigned* counters, float2* stats, int* status,
+                 cudaStream_t st) {
   (void)partials;
   (void)counters;
+  if constexpr (sizeof(act_t) == 2) {
+    // segment length: long segments amortise the two halo rows, short ones
+    // avoid dead slots when the chains are short (large dilation)
+    const int K = (m.L + dil - 1) / dil;            // longest chain
+    const int kS = K >= 64 ? 12 : (K >= 12 ? 8 : 4);
+    const int n_kb = (K + kS - 1) / kS;
+    LaunchTimer timer(kKStats, st);
+    auto go = [&](auto kern) {
+      kern<<<batch, kStatsChainThreads, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(X), convw,
+                                                 dil, m.L, m.C, n_kb, 1e-3f, stats);
+    };
+    if (m.CP == 64) {
+      if (kS == 12) go(stats_chain_kernel<64, 12>);
+      else if (kS == 8) go(stats_chain_kernel<64, 8>);
+      else go(stats_chain_kernel<64, 4>);
+    } else if (m.CP == 128) {
+      if (kS == 12) go(stats_chain_kernel<128, 12>);
+      else if (kS == 8) go(stats_chain_kernel<128, 8>);
+      else go(stats_chain_kernel<128, 4>);
+    } else {
+      return CHM_ERR_UNSUPPORTED;
+    }
+    return launch_status();
+  }
   LaunchTimer timer(kKStats, st);
   if (m.CP == 64) {
     stats_example_kernel<act_t, 64><<<batch, kStats2Threads, 0, st>>>(X, convw, dil, m.L, m.C,
@@ -328,7 +373,7 @@ int run_forward_t(const Dims& m, const PackLayout& pl, const uint8_t* packed, in
     const uint8_t* lw = packed + pl.layers + pl.layer_stride * i;
     const float* convw = reinterpret_cast<const float*>(lw + pl.l_convw);
     const int dil = 1 << i;
-    CHM_TRY(launch_stats<act_t>(m, xa, convw, dil, batch, partials, counters, stats, st));
+    CHM_TRY(launch_stats<act_t>(m, xa, convw, dil, batch, partials, counters, stats, status, st));
     MlpArgs a;
     a.X_in = xa;
     a.X_out = xb;
@@ -348,19 +393,28 @@ int run_forward_t(const Dims& m, const PackLayout& pl, const uint8_t* packed, in
   // heads
   const int cph = head_cph(m);
   const bool split_a = (m.mode == CHM_MODE_FP32);
-  if (!(cph == 256 && split_a)) {
-    HeadArgs h;
-    h.status = status;
-    h.X = xa;
-    h.X_ctl = x_ctl;
-    h.fb = packed + pl.head_pk;
-    h.fbias = reinterpret_cast<const float*>(packed + pl.head_fb);
-    h.lw = reinterpret_cast<const float*>(packed + pl.head_lw);
-    h.lbias = reinterpret_cast<const float*>(packed + pl.head_lb);
-    h.profile = profile;
-    h.logcounts = logcounts;
-    h.L = m.L; h.C = m.C; h.CP = m.CP; h.CPH = cph; h.n_ctl = m.n_ctl; h.n_out = m.n_out;
-    h.n_groups = m.n_groups; h.T = m.T; h.Lout = m.Lout;
+  HeadArgs h;
+  h.status = status;
+  h.X = xa;
+  h.X_ctl = x_ctl;
+  h.fb = packed + pl.head_pk;
+  h.fbias = reinterpret_cast<const float*>(packed + pl.head_fb);
+  h.lw = reinterpret_cast<const float*>(packed + pl.head_lw);
+  h.lbias = reinterpret_cast<const float*>(packed + pl.head_lb);
+  h.profile = profile;
+  h.logcounts = logcounts;
+  h.L = m.L; h.C = m.C; h.CP = m.CP; h.CPH = cph; h.n_ctl = m.n_ctl; h.n_out = m.n_out;
+  h.n_groups = m.n_groups; h.T = m.T; h.Lout = m.Lout;
+  if (sizeof(act_t) == 2 && m.n_ctl == 0 && m.CP == 128 && cph == 128) {
+    CUtensorMap tmap;
+    CHM_TRY(make_act_tmap3(&tmap, xa, batch, m.L, m.CP));
+    cudaFuncSetAttribute(head_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         hd2::kAlloc);
+    dim3 hgrid(m.n_out, batch);
+    LaunchTimer timer(kKProfile, st);
+    head_tma_kernel<<<hgrid, hd2::kThreads, hd2::kAlloc, st>>>(h, tmap);
+    CHM_TRY(launch_status());
+  } else if (!(cph == 256 && split_a)) {
     const int smem = head_smem_bytes(cph, split_a ? 2 : 1);
     dim3 hgrid(m.n_out, batch);
     LaunchTimer timer(kKProfile, st);
@@ -524,7 +578,8 @@ int run_block_t(const Dims& m, int batch, int dil, const uint8_t* packed, const 
   }
   if (cudaMemsetAsync(counters, 0, (size_t)batch * 4, st) != cudaSuccess) return CHM_ERR_CUDA;
   const float* convw = reinterpret_cast<const float*>(packed + pl.l_convw);
-  CHM_TRY(launch_stats<act_t>(m, xin, convw, dil, batch, partials, counters, stats, st));
+  CHM_TRY(launch_stats<act_t>(m, xin, convw, dil, batch, partials, counters, stats,
+                              reinterpret_cast<int*>(ws + bl.status), st));
   const int n_tiles = static_cast<int>((rows + kTileRows - 1) / kTileRows);
   MlpArgs a;
   a.X_in = xin;

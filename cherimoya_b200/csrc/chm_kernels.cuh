@@ -623,6 +623,107 @@ __global__ void __launch_bounds__(kStats2Threads) stats_example_kernel(
   }
 }
 
+// Per-example statistics for bf16 activations, each element read once. Row r
+// of an example belongs to the chain r = rho + k*d (rho < d); a segment is kS
+// consecutive chain positions k0 .. k0+kS-1 of one chain for one 8-channel
+// chunk, so the conv's left / centre / right operands of chain position k are
+// positions k-1, k, k+1 of the same chain: the thread loads the segment plus
+// one halo row on each side (16 B per row, a warp covers whole rows of
+// adjacent chains) and slides a three-row window through registers. The conv
+// is fp32 on paired lanes (same arithmetic as the MLP producer); each
+// segment's fp32 sums of y and y^2 fold into fp64 accumulators, and the block
+// reduction is fp64 in a fixed order (deterministic; var = E[y^2] - mean^2
+// without catastrophic cancellation).
+constexpr int kStatsChainThreads = 256;
+
+template <int CP, int kS>
+__global__ void __launch_bounds__(kStatsChainThreads, 2) stats_chain_kernel(
+    const __nv_bfloat16* __restrict__ X, const float* __restrict__ convw, int dil, int L, int C,
+    int n_kb, float eps, float2* __restrict__ stats) {
+  constexpr int kCh = CP / 8;                       // 16-byte chunks per row
+  static_assert(kStatsChainThreads % kCh == 0, "chunk count must divide the block");
+  constexpr int kSegStride = kStatsChainThreads / kCh;
+  __shared__ double red[2][kStatsChainThreads / 32];
+  const int b = blockIdx.x, tid = threadIdx.x;
+  const int ch = tid % kCh;
+  f2 w0[4], w1[4], w2[4];
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    const int c = ch * 8 + 2 * m;
+    w0[m] = f2{c < C ? convw[c] : 0.f, c + 1 < C ? convw[c + 1] : 0.f};
+    w1[m] = f2{c < C ? convw[CP + c] : 0.f, c + 1 < C ? convw[CP + c + 1] : 0.f};
+    w2[m] = f2{c < C ? convw[2 * CP + c] : 0.f, c + 1 < C ? convw[2 * CP + c + 1] : 0.f};
+  }
+  const uint4* Xb = reinterpret_cast<const uint4*>(X + (size_t)b * L * CP) + ch;
+  const int n_seg = dil * n_kb;
+  double S = 0.0, Q = 0.0;
+  for (int seg = tid / kCh; seg < n_seg; seg += kSegStride) {
+    const int kb = seg / dil;
+    const int rho = seg - kb * dil;
+    const int r0 = rho + kb * kS * dil;             // chain position k0 = kb * kS
+    if (r0 >= L) continue;
+    uint4 v[kS + 2];                                // rows r0 + (j - 1) * d
+#pragma unroll
+    for (int j = 0; j < kS + 2; ++j) {
+      const int r = r0 + (j - 1) * dil;
+      v[j] = (r >= 0 && r < L) ? __ldg(Xb + (size_t)r * kCh) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    f2 sy[4], sq[4];
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      sy[m] = f2{0.f, 0.f};
+      sq[m] = f2{0.f, 0.f};
+    }
+#pragma unroll
+    for (int j = 1; j <= kS; ++j) {
+      if (r0 + (j - 1) * dil < L) {
+        const uint32_t* pl = reinterpret_cast<const uint32_t*>(&v[j - 1]);
+        const uint32_t* pc = reinterpret_cast<const uint32_t*>(&v[j]);
+        const uint32_t* pr = reinterpret_cast<const uint32_t*>(&v[j + 1]);
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          const f2 xl{__uint_as_float(pl[m] << 16), __uint_as_float(pl[m] & 0xFFFF0000u)};
+          const f2 xc{__uint_as_float(pc[m] << 16), __uint_as_float(pc[m] & 0xFFFF0000u)};
+          const f2 xr{__uint_as_float(pr[m] << 16), __uint_as_float(pr[m] & 0xFFFF0000u)};
+          const f2 y = fma2(w0[m], xl, fma2(w1[m], xc, mul2(w2[m], xr)));
+          sy[m] = f2{sy[m].x + y.x, sy[m].y + y.y};
+          sq[m] = fma2(y, y, sq[m]);
+        }
+      }
+    }
+    const float ts = ((sy[0].x + sy[0].y) + (sy[1].x + sy[1].y)) +
+                     ((sy[2].x + sy[2].y) + (sy[3].x + sy[3].y));
+    const float tq = ((sq[0].x + sq[0].y) + (sq[1].x + sq[1].y)) +
+                     ((sq[2].x + sq[2].y) + (sq[3].x + sq[3].y));
+    S += static_cast<double>(ts);
+    Q += static_cast<double>(tq);
+  }
+  const int warp = tid >> 5, lane = tid & 31;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    S += __shfl_xor_sync(0xffffffffu, S, o);
+    Q += __shfl_xor_sync(0xffffffffu, Q, o);
+  }
+  if (lane == 0) {
+    red[0][warp] = S;
+    red[1][warp] = Q;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    double ss = 0.0, qq = 0.0;
+    for (int i = 0; i < kStatsChainThreads / 32; ++i) {
+      ss += red[0][i];
+      qq += red[1][i];
+    }
+    const double n = static_cast<double>(L) * static_cast<double>(C);
+    const double mean = ss / n;
+    double var = qq / n - mean * mean;
+    if (var < 0.0) var = 0.0;
+    stats[b] = make_float2(static_cast<float>(mean),
+                           static_cast<float>(1.0 / sqrt(var + static_cast<double>(eps))));
+  }
+}
+
 // ============================================================== MLP
 // One Cheri Block update for 128-row tiles of the flattened (B*L) rows:
 //   A1 = bf16((conv(X) - mean) * rstd)            (built by all threads)
@@ -1647,6 +1748,169 @@ __global__ void __launch_bounds__(hd::kThreads) head_kernel(HeadArgs a) {
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, 128);
+  }
+}
+
+// Profile + count head for bf16 activations without control tracks: the
+// window tiles come straight from HBM by TMA (3-D tensor map, 128-byte
+// swizzle, two boxes of 64 channels = the K-major operand layout the MMA
+// reads), so no thread touches the A operand; rows outside [0, L) arrive as
+// zero, the profile conv's padding. A is double-buffered and the TMA runs two
+// tiles ahead. Same arithmetic and fixed-order reductions as head_kernel.
+namespace hd2 {
+constexpr int kThreads = 128;
+constexpr uint32_t kBox = 128 * 128;                     // 16 KB
+constexpr uint32_t kB = 0;                               // F hi | lo: 2 x 80 x 128 bf16
+constexpr uint32_t kA = kB + 2 * hd::kNP * 128 * 2;      // 2 buffers x 2 boxes
+constexpr uint32_t kRingOff = kA + 4 * kBox;
+constexpr uint32_t kRed = kRingOff + hd::kRing * hd::kZStride * 4;
+constexpr uint32_t kBars = kRed + 512 * 4;
+constexpr uint32_t kSlot = kBars + 4 * 8;
+constexpr uint32_t kAlloc = kSlot + 16 + 1024;
+}  // namespace hd2
+
+__global__ void __launch_bounds__(hd2::kThreads) head_tma_kernel(
+    HeadArgs a, const __grid_constant__ CUtensorMap tmap) {
+  using namespace hd;
+  using hd2::kBox;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  constexpr int CPH = 128;
+  uint8_t* sB = smem + hd2::kB;
+  uint8_t* sA = smem + hd2::kA;
+  float* ring = reinterpret_cast<float*>(smem + hd2::kRingOff);
+  float* red = reinterpret_cast<float*>(smem + hd2::kRed);
+  uint64_t* a_full = reinterpret_cast<uint64_t*>(smem + hd2::kBars);     // [2]
+  uint64_t* z_full = a_full + 2;                                          // [2]
+  uint32_t* slot = reinterpret_cast<uint32_t*>(smem + hd2::kSlot);
+  const int o = blockIdx.x, b = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bool counts = (o == 0);
+  const int W = a.Lout + kHeadTaps - 1;
+  const int n_tiles = (W + kTileRows - 1) / kTileRows;
+  const int p0 = a.T - kHeadPad;
+
+  if (warp == 0) tmem_alloc(slot, 256);
+  if (tid == 0) {
+    for (int i = 0; i < 4; ++i) mbar_init(&a_full[i], 1);
+    mbar_init_fence();
+  }
+  {
+    const uint4* g = reinterpret_cast<const uint4*>(a.fb + (size_t)o * 2 * kNP * CPH * 2);
+    uint4* d = reinterpret_cast<uint4*>(sB);
+    for (int i = tid; i < 2 * kNP * CPH * 2 / 16; i += blockDim.x) d[i] = g[i];
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *slot;
+  auto load = [&](int k) {
+    const int buf = k & 1;
+    mbar_expect_tx(&a_full[buf], 2 * kBox);
+    tma_load_3d(sA + buf * 2 * kBox, &tmap, 0, p0 + k * kTileRows, b, &a_full[buf]);
+    tma_load_3d(sA + buf * 2 * kBox + kBox, &tmap, 64, p0 + k * kTileRows, b, &a_full[buf]);
+  };
+  if (tid == 0) {
+    load(0);
+    if (n_tiles > 1) load(1);
+  }
+  const uint32_t sA_addr = smem_u32(sA), sB_addr = smem_u32(sB);
+  const uint32_t idesc = idesc_bf16(kTileRows, kNP);
+  const uint32_t lane_sel = static_cast<uint32_t>(warp * 32) << 16;
+  float csum = 0.f;                      // this thread's channel (tid) over [T, L - T)
+  bool ok = true;
+  for (int k = 0; k < n_tiles; ++k) {
+    const int buf = k & 1;
+    ok = mbar_wait(&a_full[buf], (k >> 1) & 1);
+    if (__syncthreads_or(!ok)) break;
+    if (tid == 0) {
+      tc_fence_after();
+      uint32_t acc = 0;
+      for (int term = 0; term < 2; ++term) {          // F hi, F lo
+        for (int kk = 0; kk < CPH / 16; ++kk) {
+          const uint64_t da = desc_sw128(sA_addr + buf * 2 * kBox + (kk >> 2) * kBox +
+                                         (kk & 3) * 32);
+          const uint64_t db = desc_sw128(sB_addr + term * (kNP * CPH * 2) +
+                                         (kk >> 2) * (kNP * 128) + (kk & 3) * 32);
+          mma_bf16(tmem + buf * 128, da, db, idesc, acc);
+          acc = 1;
+        }
+      }
+      mma_commit(&z_full[buf]);
+    }
+    if (counts && tid < a.C) {
+      // channel tid over the tile's rows whose position lies in [T, L - T)
+      const int c = tid;
+      const uint8_t* base = sA + buf * 2 * kBox + (c >> 6) * kBox + (c & 7) * 2;
+      const int chunk = (c & 63) >> 3;
+      const int w0 = k * kTileRows;
+      for (int r = 0; r < kTileRows; ++r) {
+        const int p = p0 + w0 + r;
+        if (p >= a.T && p < a.L - a.T && w0 + r < W) {
+          const __nv_bfloat16 v =
+              *reinterpret_cast<const __nv_bfloat16*>(base + r * 128 + ((chunk ^ (r & 7)) * 16));
+          csum += __bfloat162float(v);
+        }
+      }
+    }
+    ok = mbar_wait(&z_full[buf], (k >> 1) & 1);
+    fence_async_smem();                 // generic reads of A[buf] before the refill
+    if (__syncthreads_or(!ok)) break;
+    tc_fence_after();
+    if (tid == 0 && k + 2 < n_tiles) load(k + 2);
+    // ---- Z tile -> ring rows (128k + row) mod kRing (columns 0..74)
+    {
+      const int rr = warp * 32 + lane;
+      float* zrow = ring + ((k * kTileRows + rr) % kRing) * kZStride;
+#pragma unroll 1
+      for (int part = 0; part < 3; ++part) {
+        const int col = part == 0 ? 0 : (part == 1 ? 32 : 48);   // 48..79 overlaps 32..63
+        uint32_t r[32];
+        tmem_ld32(tmem + buf * 128 + lane_sel + col, r);
+#pragma unroll
+        for (int qq = 0; qq < 32; ++qq) {
+          const int t = col + qq;
+          if ((part < 2 || t >= 64) && t < kHeadTaps) zrow[t] = __uint_as_float(r[qq]);
+        }
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+    const int j_lo = (k == 0) ? 0 : k * kTileRows - (kHeadTaps - 1);
+    const int j_hi = (k == n_tiles - 1) ? a.Lout
+                                        : min(a.Lout, k * kTileRows + kTileRows - (kHeadTaps - 1));
+    for (int j = j_lo + tid; j < j_hi; j += blockDim.x) {
+      float acc = 0.f;
+      int rrow = j % kRing;
+#pragma unroll 5
+      for (int t = 0; t < kHeadTaps; ++t) {
+        acc += ring[rrow * kZStride + t];
+        rrow = (rrow + 1 == kRing) ? 0 : rrow + 1;
+      }
+      a.profile[((long long)b * a.n_out + o) * a.Lout + j] = acc + a.fbias[o];
+    }
+    __syncthreads();
+  }
+  if (!ok && tid == 0) atomicExch(a.status, kStatusTimeout);
+  if (counts && ok) {
+    red[tid] = (tid < a.C) ? csum / static_cast<float>(a.Lout) : 0.f;
+    __syncthreads();
+    const int cin = a.C;
+    for (int g = warp; g < a.n_groups; g += blockDim.x / 32) {
+      float v = 0.f;
+      for (int c = lane; c < a.C; c += 32) v += a.lw[(long long)g * cin + c] * red[c];
+#pragma unroll
+      for (int sh = 16; sh > 0; sh >>= 1) v += __shfl_xor_sync(0xffffffffu, v, sh);
+      if (lane == 0) a.logcounts[(long long)b * a.n_groups + g] = a.lbias[g] + v;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
   }
 }
 

@@ -97,6 +97,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, 
       : "memory");
 }
 
+// 3-D tiled TMA load (no multicast); coordinates (x, y, z) innermost first.
+__device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int x, int y, int z,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // 2-D tiled TMA store from this CTA's shared memory (bulk async group).
 __device__ __forceinline__ void tma_store_2d(const void* tmap, const void* src, int x, int y) {
   asm volatile(
