@@ -347,9 +347,26 @@ int run_forward_t(const Dims& m, const PackLayout& pl, const uint8_t* packed, in
     const float* bias = reinterpret_cast<const float*>(packed + pl.stem_b);
     const uint8_t* wpk = packed + pl.stem_pk;
     const bool split = (kIn == kInDense) && m.mode == CHM_MODE_FP32;
+    LaunchTimer timer(kKStem, st);
+    if (sizeof(act_t) == 2 && m.CP == 128 && !split) {
+      // per-example tiles, TMA-stored output
+      CUtensorMap tmap;
+      CHM_TRY(make_act_tmap3(&tmap, xa, batch, m.L, m.CP));
+      const int tiles = batch * ((m.L + kTileRows - 1) / kTileRows);
+      const int tgrid = std::max(1, std::min((tiles + 1) / 2, device_sms()));
+      const int tsmem = static_cast<int>(sm2::smem_bytes(1));
+      auto go = [&](auto k) {
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, tsmem);
+        k<<<tgrid, sm2::kThreads, tsmem, st>>>(in, wpk, bias, tmap, batch, m.L, m.C, tiles,
+                                               status);
+      };
+      if (kIn == kInDense) go(stem_tc_kernel<kInDense, 1>);
+      else if (kIn == kInBases) go(stem_tc_kernel<kInBases, 1>);
+      else go(stem_tc_kernel<kInIsm, 1>);
+      CHM_TRY(launch_status());
+    } else {
     const int smem = stem_smem_bytes(m.CP, split ? 2 : 1);
     const int sgrid = std::min(n_tiles, 2 * device_sms());
-    LaunchTimer timer(kKStem, st);
 #define CHM_STEM(KIN, SPLITS)                                                             \
   do {                                                                                    \
     auto k = stem_mma_kernel<act_t, KIN, SPLITS>;                                         \
@@ -366,6 +383,7 @@ int run_forward_t(const Dims& m, const PackLayout& pl, const uint8_t* packed, in
     }
 #undef CHM_STEM
     CHM_TRY(launch_status());
+    }
   }
   // block stack
   const int grid = std::min(n_tiles, device_sms());
@@ -675,7 +693,7 @@ int32_t chm_pack_weights(const chm_model_desc* desc, const chm_params* p, void* 
   };
   CHM_TRY(copy(p->iconv_weight, pl.stem_w, (long long)m.C * 4 * kStemTaps));
   pack_sw128_split_kernel<<<(m.CP * sm::kK + 255) / 256, 256, 0, st>>>(
-      p->iconv_weight, m.C, 4 * kStemTaps, m.CP, sm::kK, dst + pl.stem_pk);
+      p->iconv_weight, m.C, 4 * kStemTaps, m.CP, sm::kK, kStemTaps, dst + pl.stem_pk);
   CHM_TRY(launch_status());
   CHM_TRY(copy(p->iconv_bias, pl.stem_b, m.C));
   for (int i = 0; i < m.n_layers; ++i) {

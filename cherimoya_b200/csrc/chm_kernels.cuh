@@ -274,7 +274,7 @@ __global__ void __launch_bounds__(256) stem_kernel(StemInput in, const float* __
 
 // ============================================================== stem, tcgen05
 // Stem as an im2col GEMM over 128-row tiles of the flattened (B*L) rows:
-//   A[r, 21k + t] = x[b, k, l + t - 10]  (K = 84, padded to 128, zero pad)
+//   A[r, 4t + k] = x[b, k, l + t - 10]  (K = 84 tap-major, padded to 128)
 //   X0[r, c] = gelu_tanh(bias[c] + sum_kk A[r, kk] W[c, kk])
 // (upstream cherimoya.py:173-174, 373). W is packed as bf16 hi + lo (two
 // MMAs carry it to ~16 bits); one-hot / base inputs are exact in bf16, a
@@ -338,7 +338,7 @@ __global__ void __launch_bounds__(sm::kThreads) stem_mma_kernel(StemInput in,
       if (rv && p >= 0 && p < L) stem_column<kIn>(in, L, b, p, col);
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        const uint32_t off = sw128_offset(tid, 21 * k + t, kTileRows);
+        const uint32_t off = sw128_offset(tid, 4 * t + k, kTileRows);
         const __nv_bfloat16 h = __float2bfloat16_rn(col[k]);
         *reinterpret_cast<__nv_bfloat16*>(sA + off) = h;
         if (kASplits > 1)
@@ -420,6 +420,184 @@ __global__ void __launch_bounds__(sm::kThreads) stem_mma_kernel(StemInput in,
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, 256);
+  }
+}
+
+// Stem for bf16 activations with C <= 128 (CP = 128): per-example tiles of
+// 128 positions (17 per 2114-bp sequence), two warpgroups per CTA, each with
+// its own tile stream, A buffer and TMEM accumulator, so one group's im2col
+// and epilogue overlap the other's. With the tap-major K order an im2col row
+// is a contiguous window of 8-byte input columns (4 channels of one
+// position): the tile's 148 columns are staged once and each row is built
+// with 16-byte stores. K = 84 needs six 16-wide MMA steps. The epilogue
+// (bias + GELU) writes the bf16 output tile into the A buffer in the
+// 128-byte-swizzled layout of a 3-D TMA box and stores it with two TMA
+// stores; positions past the end of the sequence are clipped by the tensor
+// map.
+namespace sm2 {
+constexpr int kThreads = 256;
+constexpr int kCols = kTileRows + kStemTaps - 1;   // 148 staged input columns
+constexpr int kKSteps = 6;                         // K = 84 -> 96
+constexpr int kChunks = kKSteps * 2;               // 16-byte chunks written per row
+constexpr uint32_t kW = 2 * 128 * sm::kK * 2;      // W hi | lo, 128 x 128 each
+constexpr uint32_t kA = kTileRows * sm::kK * 2;    // 32 KB
+__host__ __device__ constexpr uint32_t cols_bytes(int a_splits) {
+  return static_cast<uint32_t>(a_splits * kCols * 8);
+}
+// [W hi|lo][A group 0][A group 1][cols 0][cols 1][bias][barriers]: every
+// swizzled operand / TMA box starts on a 1024-byte boundary
+__host__ __device__ constexpr uint32_t cols_off(int a_splits) { return kW + 2 * a_splits * kA; }
+__host__ __device__ constexpr uint32_t cols_stride(int a_splits) {
+  return (cols_bytes(a_splits) + 127) & ~127u;
+}
+__host__ __device__ constexpr uint32_t smem_bytes(int a_splits) {
+  return cols_off(a_splits) + 2 * cols_stride(a_splits) + 128 * 4 + 64 + 1024;
+}
+static_assert(kW % 1024 == 0 && kA % 1024 == 0, "swizzled buffers need 1024-byte alignment");
+}  // namespace sm2
+
+__device__ __forceinline__ uint2 bf16x4_hi(const float (&v)[4]) {
+  return make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]));
+}
+
+template <int kIn, int kASplits>
+__global__ void __launch_bounds__(sm2::kThreads, 1) stem_tc_kernel(
+    StemInput in, const uint8_t* __restrict__ wpk, const float* __restrict__ bias,
+    const __grid_constant__ CUtensorMap tmap, int batch, int L, int C, int n_tiles,
+    int* status) {
+  using namespace sm2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int g = tid >> 7, gt = tid & 127;            // warpgroup, row within the tile
+  uint8_t* sB = smem;
+  uint8_t* sA = smem + kW + g * kASplits * kA;       // [kASplits] 128 x 128 bf16
+  uint2* cols = reinterpret_cast<uint2*>(smem + cols_off(kASplits) +
+                                         g * cols_stride(kASplits));   // [kASplits][kCols]
+  float* sbias = reinterpret_cast<float*>(smem + cols_off(kASplits) + 2 * cols_stride(kASplits));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sbias + 128);    // [2]
+  uint32_t* slot = reinterpret_cast<uint32_t*>(bar + 2);
+  if (warp == 0) tmem_alloc(slot, 256);
+  if (tid == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    mbar_init_fence();
+  }
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(wpk);
+    uint4* dst = reinterpret_cast<uint4*>(sB);
+    for (int i = tid; i < static_cast<int>(kW / 16); i += blockDim.x) dst[i] = src[i];
+    if (tid < 128) sbias[tid] = tid < C ? bias[tid] : 0.f;
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *slot + g * 128;
+  const uint32_t sA_addr = smem_u32(sA), sB_addr = smem_u32(sB);
+  const uint32_t idesc = idesc_bf16(kTileRows, 128);
+  const uint32_t lane_sel = static_cast<uint32_t>((warp & 3) * 32) << 16;
+  const int tpe = (L + kTileRows - 1) / kTileRows;
+  const uint32_t bar_id = 1 + g;
+  uint32_t it = 0;
+  bool ok = true;
+  for (int tile = blockIdx.x * 2 + g; tile < n_tiles; tile += gridDim.x * 2, ++it) {
+    const int b = tile / tpe;
+    const int l0 = (tile - b * tpe) * kTileRows;
+    // ---- stage input columns l0 - 10 .. l0 + 137 (zero outside [0, L))
+    for (int i = gt; i < kCols; i += 128) {
+      const int p = l0 + i - kStemPad;
+      float col[4] = {0.f, 0.f, 0.f, 0.f};
+      if (p >= 0 && p < L) stem_column<kIn>(in, L, b, p, col);
+      const uint2 h = bf16x4_hi(col);
+      cols[i] = h;
+      if (kASplits > 1) {
+        const float lo[4] = {col[0] - __uint_as_float(h.x << 16),
+                             col[1] - __uint_as_float(h.x & 0xFFFF0000u),
+                             col[2] - __uint_as_float(h.y << 16),
+                             col[3] - __uint_as_float(h.y & 0xFFFF0000u)};
+        cols[kCols + i] = bf16x4_hi(lo);
+      }
+    }
+    if (gt == 0) bulk_wait_read0();     // the previous output tile has left sA
+    named_sync(bar_id, 128);
+    // ---- im2col row gt: chunk q = taps 2q, 2q+1 (tap 21 = zero)
+#pragma unroll
+    for (int sp = 0; sp < kASplits; ++sp) {
+      const uint2* cs = cols + sp * kCols + gt;
+      uint8_t* dst = sA + sp * kA;
+#pragma unroll
+      for (int q = 0; q < kChunks; ++q) {
+        const uint2 a = (2 * q < kStemTaps) ? cs[2 * q] : make_uint2(0u, 0u);
+        const uint2 c = (2 * q + 1 < kStemTaps) ? cs[2 * q + 1] : make_uint2(0u, 0u);
+        *reinterpret_cast<uint4*>(dst + sw128_offset(gt, 8 * q, kTileRows)) =
+            make_uint4(a.x, a.y, c.x, c.y);
+      }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    named_sync(bar_id, 128);
+    if (gt == 0) {
+      tc_fence_after();
+      uint32_t acc = 0;
+      for (int term = 0; term < (kASplits > 1 ? 3 : 2); ++term) {
+        const int ai = (term == 2) ? 1 : 0;
+        const int bi = (term == 1) ? 1 : 0;
+#pragma unroll
+        for (int kk = 0; kk < kKSteps; ++kk) {
+          const uint64_t da = desc_sw128(sA_addr + ai * kA + (kk >> 2) * (kTileRows * 128) +
+                                         (kk & 3) * 32);
+          const uint64_t db = desc_sw128(sB_addr + bi * (kW / 2) + (kk >> 2) * (128 * 128) +
+                                         (kk & 3) * 32);
+          mma_bf16(tmem, da, db, idesc, acc);
+          acc = 1;
+        }
+      }
+      mma_commit(&bar[g]);
+    }
+    ok = mbar_wait(&bar[g], it & 1);
+    if (!ok) {
+      if (gt == 0) atomicExch(status, kStatusTimeout);
+      break;
+    }
+    tc_fence_after();
+    // ---- bias + GELU -> bf16 output tile in sA (two 64-channel boxes)
+#pragma unroll 1
+    for (int j = 0; j < 4; ++j) {
+      uint32_t d[32];
+      tmem_ld32(tmem + lane_sel + j * 32, d);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int c = j * 32 + q * 8 + 2 * e;
+          const float z0 = __uint_as_float(d[q * 8 + 2 * e]) + sbias[c];
+          const float z1 = __uint_as_float(d[q * 8 + 2 * e + 1]) + sbias[c + 1];
+          const float y0 = (c < C) ? gelu_tanh<true>(z0) : 0.f;
+          const float y1 = (c + 1 < C) ? gelu_tanh<true>(z1) : 0.f;
+          pk[e] = pack_bf16x2(y0, y1);
+        }
+        *reinterpret_cast<uint4*>(sA + sw128_offset(gt, j * 32 + q * 8, kTileRows)) =
+            make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    named_sync(bar_id, 128);
+    if (gt == 0) {
+      tma_store_3d(&tmap, sA, 0, l0, b);
+      tma_store_3d(&tmap, sA + kTileRows * 128, 64, l0, b);
+      bulk_commit();
+    }
+  }
+  if (gt == 0) bulk_wait0();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(*slot, 256);
   }
 }
 
@@ -2076,12 +2254,19 @@ __global__ void pack_sw128_kernel(const float* __restrict__ src, int R, int K, i
 
 // hi / lo split of an fp32 (R, K) matrix into two bf16 swizzled tiles
 // (lo = value - bf16(value)); dst holds [hi | lo], each RP x KP.
+// taps > 0: src rows are (channels x taps) channel-major and the packed K
+// order is tap-major, k = channels * t + c  <-  src column taps * c + t.
 __global__ void pack_sw128_split_kernel(const float* __restrict__ src, int R, int K, int RP,
-                                        int KP, uint8_t* __restrict__ dst) {
+                                        int KP, int taps, uint8_t* __restrict__ dst) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= RP * KP) return;
   const int r = i / KP, k = i - (i / KP) * KP;
-  const float v = (r < R && k < K) ? src[(long long)r * K + k] : 0.f;
+  int ks = k;
+  if (taps > 0 && k < K) {
+    const int chans = K / taps;
+    ks = (k % chans) * taps + k / chans;
+  }
+  const float v = (r < R && k < K) ? src[(long long)r * K + ks] : 0.f;
   const __nv_bfloat16 h = __float2bfloat16_rn(v);
   const uint32_t off = sw128_offset(r, k, RP);
   *reinterpret_cast<__nv_bfloat16*>(dst + off) = h;

@@ -115,6 +115,16 @@ __device__ __forceinline__ void tma_store_2d(const void* tmap, const void* src, 
       "r"(smem_u32(src)), "r"(x), "r"(y)
       : "memory");
 }
+// 3-D tiled TMA store (bulk async group); elements outside the tensor are
+// not written.
+__device__ __forceinline__ void tma_store_3d(const void* tmap, const void* src, int x, int y,
+                                             int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(tmap)),
+      "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
 __device__ __forceinline__ void bulk_commit() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
