@@ -1215,10 +1215,21 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
     uint4* s2 = reinterpret_cast<uint4*>(smem + kW2);
     for (int i = tid; i < kH * kC * 2 / 16; i += blockDim.x) s1[i] = g1[i];
     for (int i = tid; i < kC * kH * 2 / 16; i += blockDim.x) s2[i] = g2[i];
-    float* cw = reinterpret_cast<float*>(smem + kConvW);
-    for (int i = tid; i < 3 * kC; i += blockDim.x) {
-      const int c = i % kC;
-      cw[i] = (c < a.C) ? a.convw[i] : 0.f;
+    if constexpr (sizeof(act_t) == 2) {
+      // bf16 activations: conv weights as bf16x2 channel pairs [tap][pair]
+      uint32_t* cw = reinterpret_cast<uint32_t*>(smem + kConvW);
+      for (int i = tid; i < 3 * kC / 2; i += blockDim.x) {
+        const int t = i / (kC / 2), c = 2 * (i % (kC / 2));
+        const float v0 = (c < a.C) ? a.convw[t * kC + c] : 0.f;
+        const float v1 = (c + 1 < a.C) ? a.convw[t * kC + c + 1] : 0.f;
+        cw[i] = pack_bf16x2(v0, v1);
+      }
+    } else {
+      float* cw = reinterpret_cast<float*>(smem + kConvW);
+      for (int i = tid; i < 3 * kC; i += blockDim.x) {
+        const int c = i % kC;
+        cw[i] = (c < a.C) ? a.convw[i] : 0.f;
+      }
     }
   }
   fence_async_smem();
@@ -1251,6 +1262,8 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       }
       const f2 scale2{st.y, st.y};
       const f2 shift2{-st.x * st.y, -st.x * st.y};
+      const uint32_t scale_b = pack_bf16x2(st.y, st.y);
+      const uint32_t shift_b = pack_bf16x2(-st.x * st.y, -st.x * st.y);
       const bool hasL = rv && (l - a.dil >= 0), hasR = rv && (l + a.dil < a.L);
       for (int b = 0; b < kBoxes; ++b, ++k) {
         const int slotk = k & 1;
@@ -1269,6 +1282,37 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
         const uint8_t* bR = bL + 2 * kBox;
         const int cbase = b * kBoxCh;              // first channel of the box
         uint32_t packed[kBoxCh / 2];
+        if constexpr (sizeof(act_t) == 2) {
+          // bf16x2 conv + LayerNorm: y = w0 xl + w1 xc + w2 xr, a = y rstd - mean rstd,
+          // four packed operations per channel pair, no unpacking
+          const uint32_t* cw2 = reinterpret_cast<const uint32_t*>(smem + kConvW);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t off = static_cast<uint32_t>((q ^ ((rl >> 1) & 3)) * 16);
+            uint4 vl = *reinterpret_cast<const uint4*>(bL + off);
+            const uint4 vc = *reinterpret_cast<const uint4*>(bC + off);
+            uint4 vr = *reinterpret_cast<const uint4*>(bR + off);
+            if (!hasL) vl = make_uint4(0, 0, 0, 0);
+            if (!hasR) vr = make_uint4(0, 0, 0, 0);
+            const int pr = (cbase + q * 8) / 2;    // first channel pair of the chunk
+            const uint4 w0 = *reinterpret_cast<const uint4*>(cw2 + pr);
+            const uint4 w1 = *reinterpret_cast<const uint4*>(cw2 + kC / 2 + pr);
+            const uint4 w2 = *reinterpret_cast<const uint4*>(cw2 + kC + pr);
+            const uint32_t* pl = &vl.x;
+            const uint32_t* pc = &vc.x;
+            const uint32_t* pq = &vr.x;
+            const uint32_t* p0 = &w0.x;
+            const uint32_t* p1 = &w1.x;
+            const uint32_t* p2 = &w2.x;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              uint32_t y = bf2_mul(p2[e], pq[e]);
+              y = bf2_fma(p1[e], pc[e], y);
+              y = bf2_fma(p0[e], pl[e], y);
+              packed[q * 4 + e] = bf2_fma(y, scale_b, shift_b);
+            }
+          }
+        } else {
 #pragma unroll
         for (int q = 0; q < 4; ++q) {              // 16-byte chunks of the row
           const uint32_t off = static_cast<uint32_t>((q ^ ((rl >> 1) & 3)) * 16);
@@ -1299,6 +1343,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
             packed[(q * kE + e) / 2] = pack_bf16x2(y0.x, y0.y);
             packed[(q * kE + e) / 2 + 1] = pack_bf16x2(y1.x, y1.y);
           }
+        }
         }
         if (!rv) {
 #pragma unroll

@@ -324,6 +324,18 @@ __device__ __forceinline__ uint32_t gelu_bf16x2(float z0, float z1) {
   return g;
 }
 
+// Packed bf16x2 arithmetic: one rounding to bf16 per operation.
+__device__ __forceinline__ uint32_t bf2_fma(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ uint32_t bf2_mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
 // Packed fp32x2 arithmetic (sm_100): two fp32 lanes per instruction.
 struct f2 {
   float x, y;
