@@ -1248,22 +1248,33 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
     const uint32_t lane_sel = static_cast<uint32_t>(quarter * 32) << 16;
     uint32_t k = 0;
     bool ok = true;
+    // statistics of this thread's row in tile `it`, loaded one tile ahead
+    auto row_stats = [&](int it2, int& l2) -> float2 {
+      const long long r2 = (long long)(first + it2 * stride) * kTileRows + rl;
+      l2 = 0;
+      if (it2 >= n_my || r2 >= a.rows) return make_float2(0.f, 0.f);
+      const int n2 = static_cast<int>(r2 / a.L);
+      l2 = static_cast<int>(r2 - (long long)n2 * a.L);
+      return a.stats[n2];
+    };
+    int l_next;
+    float2 st_next = row_stats(0, l_next);
     for (int it = 0; it < n_my && ok; ++it) {
       const int buf = it & 1;
       const long long row0 = (long long)(first + it * stride) * kTileRows;
       const long long r = row0 + rl;
       const bool rv = r < a.rows;
-      int l = 0;
-      float2 st = make_float2(0.f, 0.f);
-      if (rv) {
-        const int n = static_cast<int>(r / a.L);
-        l = static_cast<int>(r - (long long)n * a.L);
-        st = a.stats[n];
-      }
+      const int l = l_next;
+      const float2 st = st_next;
+      st_next = row_stats(it + 1, l_next);
       const f2 scale2{st.y, st.y};
       const f2 shift2{-st.x * st.y, -st.x * st.y};
-      const uint32_t scale_b = pack_bf16x2(st.y, st.y);
-      const uint32_t shift_b = pack_bf16x2(-st.x * st.y, -st.x * st.y);
+      // bf16 fast path: A1 carries a factor 1/2 (exact), which the GELU of
+      // D1 / 2 expects (gelu_half_bf16x2)
+      constexpr float kA1Scale = (sizeof(act_t) == 2 && kFastGelu) ? 0.5f : 1.0f;
+      const uint32_t scale_b = pack_bf16x2(kA1Scale * st.y, kA1Scale * st.y);
+      const uint32_t shift_b =
+          pack_bf16x2(-kA1Scale * st.x * st.y, -kA1Scale * st.x * st.y);
       const bool hasL = rv && (l - a.dil >= 0), hasR = rv && (l + a.dil < a.L);
       for (int b = 0; b < kBoxes; ++b, ++k) {
         const int slotk = k & 1;
@@ -1286,14 +1297,24 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
           // bf16x2 conv + LayerNorm: y = w0 xl + w1 xc + w2 xr, a = y rstd - mean rstd,
           // four packed operations per channel pair, no unpacking
           const uint32_t* cw2 = reinterpret_cast<const uint32_t*>(smem + kConvW);
+          uint4 sl[4], sc[4], sr[4];
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const uint32_t off = static_cast<uint32_t>((q ^ ((rl >> 1) & 3)) * 16);
-            uint4 vl = *reinterpret_cast<const uint4*>(bL + off);
-            const uint4 vc = *reinterpret_cast<const uint4*>(bC + off);
-            uint4 vr = *reinterpret_cast<const uint4*>(bR + off);
-            if (!hasL) vl = make_uint4(0, 0, 0, 0);
-            if (!hasR) vr = make_uint4(0, 0, 0, 0);
+            sl[q] = *reinterpret_cast<const uint4*>(bL + off);
+            sc[q] = *reinterpret_cast<const uint4*>(bC + off);
+            sr[q] = *reinterpret_cast<const uint4*>(bR + off);
+          }
+          // the row is in registers: release the slot now so its refill
+          // overlaps the arithmetic (proxy fence: generic reads before the
+          // TMA overwrites the slot)
+          fence_async_smem();
+          mbar_arrive(&bars[STG_EMPTY0 + slotk]);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint4 vl = hasL ? sl[q] : make_uint4(0, 0, 0, 0);
+            const uint4 vc = sc[q];
+            const uint4 vr = hasR ? sr[q] : make_uint4(0, 0, 0, 0);
             const int pr = (cbase + q * 8) / 2;    // first channel pair of the chunk
             const uint4 w0 = *reinterpret_cast<const uint4*>(cw2 + pr);
             const uint4 w1 = *reinterpret_cast<const uint4*>(cw2 + kC / 2 + pr);
@@ -1349,12 +1370,14 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
 #pragma unroll
           for (int e = 0; e < kBoxCh / 2; ++e) packed[e] = 0u;
         }
-        // staging consumed: release the slot (the TMA warp refills it with
-        // box k + 2). The proxy fence orders these generic-proxy reads before
-        // the TMA (async proxy) overwrites the slot; without it the refill
-        // can land before the reads complete.
-        fence_async_smem();
-        mbar_arrive(&bars[STG_EMPTY0 + slotk]);
+        if constexpr (sizeof(act_t) != 2) {
+          // staging consumed: release the slot (the TMA warp refills it with
+          // box k + 2). The proxy fence orders these generic-proxy reads
+          // before the TMA (async proxy) overwrites the slot; without it the
+          // refill can land before the reads complete.
+          fence_async_smem();
+          mbar_arrive(&bars[STG_EMPTY0 + slotk]);
+        }
         // packed channels [cbase, cbase + kBoxCh) -> A1 columns cbase / 2 ...
         const uint32_t col = tmem + lane_sel + kA1Col + buf * 64 + cbase / 2;
         if constexpr (kBoxCh / 2 == 16) {
@@ -1394,7 +1417,9 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
           uint32_t p[16];
 #pragma unroll
           for (int q = 0; q < 16; ++q) {
-            if constexpr (kFastGelu) {
+            if constexpr (kFastGelu && sizeof(act_t) == 2) {
+              p[q] = gelu_half_bf16x2(__uint_as_float(r[2 * q]), __uint_as_float(r[2 * q + 1]));
+            } else if constexpr (kFastGelu) {
               p[q] = gelu_bf16x2(__uint_as_float(r[2 * q]), __uint_as_float(r[2 * q + 1]));
             } else {
               p[q] = pack_bf16x2(gelu_tanh<false>(__uint_as_float(r[2 * q])),
@@ -1424,7 +1449,14 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
           for (int q = 0; q < 4; ++q) {
             const int chunk = j * 4 + q;                  // 8 channels per chunk
             uint4* ptr = reinterpret_cast<uint4*>(rowp + ((chunk ^ (rl & 7)) * 16));
-            *ptr = add_residual<act_t>(*ptr, d + q * 8);
+            const uint4 x = *ptr;
+            const uint32_t* dq = d + q * 8;
+            // x + bf16(D2) in bf16x2 (one extra rounding of the update)
+            *ptr = make_uint4(
+                bf2_add(x.x, pack_bf16x2(__uint_as_float(dq[0]), __uint_as_float(dq[1]))),
+                bf2_add(x.y, pack_bf16x2(__uint_as_float(dq[2]), __uint_as_float(dq[3]))),
+                bf2_add(x.z, pack_bf16x2(__uint_as_float(dq[4]), __uint_as_float(dq[5]))),
+                bf2_add(x.w, pack_bf16x2(__uint_as_float(dq[6]), __uint_as_float(dq[7]))));
           }
         }
         tc_fence_before();

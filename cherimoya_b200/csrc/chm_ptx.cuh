@@ -336,6 +336,29 @@ __device__ __forceinline__ uint32_t bf2_mul(uint32_t a, uint32_t b) {
   return d;
 }
 
+__device__ __forceinline__ uint32_t bf2_add(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// gelu_bf16x2 of 2 h0, 2 h1 given h = x / 2 (the pre-activation carries the
+// factor 1/2): u = h (2 k0 + 8 k1 h^2) = x (k0 + k1 x^2), result h + h tanh(u).
+// Every rounding sees the same value as in gelu_bf16x2 scaled by a power of
+// two, so the results are identical, with one multiply fewer.
+__device__ __forceinline__ uint32_t gelu_half_bf16x2(float h0, float h1) {
+  uint32_t hx, sq, t, u, th, g;
+  asm("cvt.rn.bf16x2.f32 %0, %2, %1;" : "=r"(hx) : "f"(h0), "f"(h1));
+  const uint32_t k1 = 0x3E923E92u;   // 8 * bf16x2(0.0356774)
+  const uint32_t k0 = 0x3FCC3FCCu;   // 2 * bf16x2(0.7978846)
+  asm("mul.rn.bf16x2 %0, %1, %1;" : "=r"(sq) : "r"(hx));
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(t) : "r"(sq), "r"(k1), "r"(k0));
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(u) : "r"(hx), "r"(t));
+  asm("tanh.approx.bf16x2 %0, %1;" : "=r"(th) : "r"(u));
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(g) : "r"(hx), "r"(th), "r"(hx));
+  return g;
+}
+
 // Packed fp32x2 arithmetic (sm_100): two fp32 lanes per instruction.
 struct f2 {
   float x, y;
