@@ -1148,10 +1148,11 @@ __global__ void __launch_bounds__(128, 1) mlp_kernel(MlpArgs a) {
 // tile 32 KB, conv weights.
 namespace ws {
 constexpr int kC = 128, kH = 256, kHalf = 128;
-constexpr int kProducerWarps = 4, kEpilogueWarps = 8;
-constexpr int kMmaWarp = kProducerWarps + kEpilogueWarps;      // 12
-constexpr int kTmaWarp = kMmaWarp + 1;                          // 13
-constexpr int kThreads = (kTmaWarp + 1) * 32;                   // 448
+constexpr int kProducerWarps = 4, kEpilogueWarps = 8, kResidualWarps = 4;
+constexpr int kResidualWarp0 = kProducerWarps + kEpilogueWarps; // 12
+constexpr int kMmaWarp = kResidualWarp0 + kResidualWarps;       // 16
+constexpr int kTmaWarp = kMmaWarp + 1;                          // 17
+constexpr int kThreads = (kTmaWarp + 1) * 32;                   // 576
 constexpr uint32_t kBoxBytes = 64;                              // staging box row width
 constexpr uint32_t kBox = kBoxBytes * 128;                      // 8 KB staging box
 constexpr uint32_t kResBox = 128 * 128;                         // 16 KB residual box
@@ -1164,7 +1165,7 @@ constexpr uint32_t kConvW = kRes + 2 * kResBox;                 // 3 x 128 fp32
 constexpr uint32_t kBars = kConvW + 3 * kC * 4;
 enum Bar { STG_FULL0, STG_FULL1, STG_EMPTY0, STG_EMPTY1, A1_FULL0, A1_FULL1, A1_EMPTY0,
            A1_EMPTY1, D1A_FULL, D1B_FULL, A2A_FULL, A2B_FULL, D2_FULL, RES_FULL, RES_DONE,
-           kNumBars };
+           D2_EMPTY, kNumBars };
 constexpr uint32_t kSlot = kBars + kNumBars * 8;
 constexpr uint32_t kAbort = kSlot + 4;
 constexpr uint32_t kBytes = kAbort + 4;
@@ -1203,7 +1204,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
     const uint32_t counts[kNumBars] = {1, 1, kProducerWarps * 32, kProducerWarps * 32,
                                        kProducerWarps * 32, kProducerWarps * 32, 1, 1, 1, 1,
                                        kEpilogueWarps * 32, kEpilogueWarps * 32, 1, 1,
-                                       kEpilogueWarps * 32};
+                                       kResidualWarps * 32, kResidualWarps * 32};
     for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], counts[i]);
     *abort_flag = 0;
     mbar_init_fence();
@@ -1253,8 +1254,15 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       const long long r2 = (long long)(first + it2 * stride) * kTileRows + rl;
       l2 = 0;
       if (it2 >= n_my || r2 >= a.rows) return make_float2(0.f, 0.f);
-      const int n2 = static_cast<int>(r2 / a.L);
-      l2 = static_cast<int>(r2 - (long long)n2 * a.L);
+      int n2;
+      if (a.rows < (1LL << 31)) {
+        const uint32_t u = static_cast<uint32_t>(r2);
+        n2 = static_cast<int>(u / static_cast<uint32_t>(a.L));
+        l2 = static_cast<int>(u - static_cast<uint32_t>(n2) * static_cast<uint32_t>(a.L));
+      } else {
+        n2 = static_cast<int>(r2 / a.L);
+        l2 = static_cast<int>(r2 - (long long)n2 * a.L);
+      }
       return a.stats[n2];
     };
     int l_next;
@@ -1392,16 +1400,14 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       tc_fence_before();
       mbar_arrive(&bars[A1_FULL0 + buf]);
     }
-  } else if (warp < kMmaWarp) {
-    // ------------------------------------------------------------ epilogue
+  } else if (warp < kResidualWarp0) {
+    // ------------------------------------------------------------ GELU epilogue
     const int ew = warp - kProducerWarps;          // 0..7
     const int quarter = warp & 3;                  // TMEM lane quarter of this warp
     const int g = ew >> 2;                         // warpgroup: half columns [64g, 64g+64)
     const int rl = quarter * 32 + lane;            // tile row of this thread
     const uint32_t lane_sel = static_cast<uint32_t>(quarter * 32) << 16;
-    uint8_t* sRes = smem + kRes;
     for (int it = 0; it < n_my; ++it) {
-      const long long row0 = (long long)(first + it * stride) * kTileRows;
       bool ok = true;
 #pragma unroll 1
       for (int hh = 0; hh < 2; ++hh) {
@@ -1433,47 +1439,87 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
         mbar_arrive(&bars[hh ? A2B_FULL : A2A_FULL]);
       }
       if (!ok) break;
-      const long long r = row0 + rl;
-      const bool rv = r < a.rows;
+    }
+  } else if (warp < kMmaWarp) {
+    // ------------------------------------------------------------ residual epilogue
+    // X_out = X_in + D2 for whole rows (thread = row, all channels); D2 is
+    // released (D2_EMPTY) as soon as it has been read, before the tile store
+    const int quarter = warp & 3;
+    const int rl = quarter * 32 + lane;
+    const uint32_t lane_sel = static_cast<uint32_t>(quarter * 32) << 16;
+    uint8_t* sRes = smem + kRes;
+    for (int it = 0; it < n_my; ++it) {
       if constexpr (kTmaResidual) {
         // residual of D2 through the TMA-loaded input tile, in place
+        // the tile's input rows arrive by TMA (issued by this group's leader
+        // after the previous tile's store left the buffer)
+        const bool leader = (warp == kResidualWarp0 && lane == 0);
+        auto load_res = [&](int tit) {
+          const int y0 = (first + tit * stride) * kTileRows;
+          mbar_expect_tx(&bars[RES_FULL], 2 * kResBox);
+          tma_load_2d(sRes, &maps.res, 0, y0, &bars[RES_FULL]);
+          tma_load_2d(sRes + kResBox, &maps.res, 64, y0, &bars[RES_FULL]);
+        };
+        if (it == 0 && leader) load_res(0);
         if (!mbar_wait_abortable(&bars[RES_FULL], it & 1, abort_flag)) break;
         if (!mbar_wait_abortable(&bars[D2_FULL], it & 1, abort_flag)) break;
         tc_fence_after();
-        uint8_t* rowp = sRes + g * kResBox + rl * 128;   // this thread's 64 channels
+#pragma unroll 1
+        for (int jj = 0; jj < 4; ++jj) {
+          const int g = jj >> 1, j = jj & 1;
+          uint8_t* rowp = sRes + g * kResBox + rl * 128;   // channels [64g, 64g + 64)
+          uint4 x[4];
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
+          for (int q = 0; q < 4; ++q)                     // 8 channels per chunk
+            x[q] = *reinterpret_cast<const uint4*>(rowp + (((j * 4 + q) ^ (rl & 7)) * 16));
           uint32_t d[32];
-          tmem_ld32(tmem + lane_sel + kD2Col + g * 64 + j * 32, d);
+          tmem_ld32(tmem + lane_sel + kD2Col + jj * 32, d);
+          if (jj == 3) {
+            tc_fence_before();
+            mbar_arrive(&bars[D2_EMPTY]);                 // D2 fully read
+          }
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            const int chunk = j * 4 + q;                  // 8 channels per chunk
-            uint4* ptr = reinterpret_cast<uint4*>(rowp + ((chunk ^ (rl & 7)) * 16));
-            const uint4 x = *ptr;
             const uint32_t* dq = d + q * 8;
             // x + bf16(D2) in bf16x2 (one extra rounding of the update)
-            *ptr = make_uint4(
-                bf2_add(x.x, pack_bf16x2(__uint_as_float(dq[0]), __uint_as_float(dq[1]))),
-                bf2_add(x.y, pack_bf16x2(__uint_as_float(dq[2]), __uint_as_float(dq[3]))),
-                bf2_add(x.z, pack_bf16x2(__uint_as_float(dq[4]), __uint_as_float(dq[5]))),
-                bf2_add(x.w, pack_bf16x2(__uint_as_float(dq[6]), __uint_as_float(dq[7]))));
+            *reinterpret_cast<uint4*>(rowp + (((j * 4 + q) ^ (rl & 7)) * 16)) = make_uint4(
+                bf2_add(x[q].x, pack_bf16x2(__uint_as_float(dq[0]), __uint_as_float(dq[1]))),
+                bf2_add(x[q].y, pack_bf16x2(__uint_as_float(dq[2]), __uint_as_float(dq[3]))),
+                bf2_add(x[q].z, pack_bf16x2(__uint_as_float(dq[4]), __uint_as_float(dq[5]))),
+                bf2_add(x[q].w, pack_bf16x2(__uint_as_float(dq[6]), __uint_as_float(dq[7]))));
           }
         }
-        tc_fence_before();
         fence_async_smem();                               // generic writes -> TMA store
-        mbar_arrive(&bars[RES_DONE]);                     // the TMA warp stores the tile
+        mbar_arrive(&bars[RES_DONE]);
+        if (leader) {
+          if (!mbar_wait_abortable(&bars[RES_DONE], it & 1, abort_flag)) break;
+          const int y0 = (first + it * stride) * kTileRows;
+          tma_store_2d(&maps.out, sRes, 0, y0);
+          tma_store_2d(&maps.out, sRes + kResBox, 64, y0);
+          bulk_commit();
+          if (it + 1 < n_my) {
+            bulk_wait_read0();                            // the tile buffer is free again
+            load_res(it + 1);
+          } else {
+            bulk_wait0();                                 // stores complete before exit
+          }
+        }
       } else {
         // residual of D2 on rows read directly from global memory (fp32)
+        const long long r = (long long)(first + it * stride) * kTileRows + rl;
+        const bool rv = r < a.rows;
         constexpr int kVE = 16 / sizeof(act_t);
         constexpr int kPre = 32 / kVE;
+        if (!mbar_wait_abortable(&bars[D2_FULL], it & 1, abort_flag)) break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int g = 0; g < 2; ++g) {
         const act_t* xrow = Xi + r * kC + g * 64;
         act_t* orow = Xo + r * kC + g * 64;
         uint4 xin[kPre];
 #pragma unroll
         for (int q = 0; q < kPre; ++q)
           xin[q] = rv ? *reinterpret_cast<const uint4*>(xrow + q * kVE) : make_uint4(0, 0, 0, 0);
-        if (!mbar_wait_abortable(&bars[D2_FULL], it & 1, abort_flag)) break;
-        tc_fence_after();
 #pragma unroll 1
         for (int j = 0; j < 2; ++j) {
           uint32_t d[32];
@@ -1491,10 +1537,10 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
                   add_residual<act_t>(xin[q], d + q * kVE);
           }
         }
+        }
         tc_fence_before();
+        mbar_arrive(&bars[D2_EMPTY]);
       }
-      // D2 is next written by G2a(t+1), which the MMA issues only after this
-      // warpgroup's GELU of tile t+1: program order protects it.
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
@@ -1533,6 +1579,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
         const bool next = it + 1 < n_my;
         const int nbuf = (it + 1) & 1;
         ok = mbar_wait_abortable(&bars[A2A_FULL], it & 1, abort_flag);
+        if (ok && it > 0) ok = mbar_wait_abortable(&bars[D2_EMPTY], (it - 1) & 1, abort_flag);
         if (!ok) break;
         tc_fence_after();
         g2(0);
@@ -1586,41 +1633,16 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
           tma_load_2d(smem + kStg + (slotk * 3 + blk) * kBox, &maps.stage, b * kBoxCh,
                       y0 + (blk - 1) * a.dil, &bars[STG_FULL0 + slotk]);
       };
-      auto load_res = [&](int tit) {
-        mbar_expect_tx(&bars[RES_FULL], 2 * kResBox);
-        const int y0 = (first + tit * stride) * kTileRows;
-        tma_load_2d(smem + kRes, &maps.res, 0, y0, &bars[RES_FULL]);
-        tma_load_2d(smem + kRes + kResBox, &maps.res, 64, y0, &bars[RES_FULL]);
-      };
       const uint32_t n_steps = static_cast<uint32_t>(n_my) * kBoxes;
       issue(0);
       if (n_steps > 1) issue(1);
-      if (kTmaResidual) load_res(0);
       uint32_t k_next = 2;                 // next staging box step to issue
-      int r_next = kTmaResidual ? 0 : n_my; // next residual tile to store
       const uint64_t t0 = global_ns();
       uint64_t last_progress = t0;
-      for (uint32_t spin = 0; k_next < n_steps || r_next < n_my; ++spin) {
-        bool progress = false;
-        if (k_next < n_steps &&
-            mbar_try(smem_u32(&bars[STG_EMPTY0 + (k_next & 1)]), ((k_next - 2) >> 1) & 1)) {
+      for (uint32_t spin = 0; k_next < n_steps; ++spin) {
+        if (mbar_try(smem_u32(&bars[STG_EMPTY0 + (k_next & 1)]), ((k_next - 2) >> 1) & 1)) {
           issue(k_next);
           ++k_next;
-          progress = true;
-        }
-        if (r_next < n_my && mbar_try(smem_u32(&bars[RES_DONE]), r_next & 1)) {
-          const int y0 = (first + r_next * stride) * kTileRows;
-          tma_store_2d(&maps.out, smem + kRes, 0, y0);
-          tma_store_2d(&maps.out, smem + kRes + kResBox, 64, y0);
-          bulk_commit();
-          if (r_next + 1 < n_my) {
-            bulk_wait_read0();             // the tile buffer is free again
-            load_res(r_next + 1);
-          }
-          ++r_next;
-          progress = true;
-        }
-        if (progress) {
           last_progress = global_ns();
         } else if ((spin & 255u) == 255u) {
           if (*abort_flag || global_ns() - last_progress > kWaitNs) {
@@ -1629,12 +1651,11 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
           }
         }
       }
-      bulk_wait0();                        // residual stores complete before exit
     }
     __syncwarp();
   }
-  // drain: every MMA this CTA issued has been waited on by the epilogue
-  // (D2_FULL of the last tile) unless the pipeline aborted.
+  // drain: every MMA this CTA issued has been waited on by the residual
+  // warps (D2_FULL of the last tile) unless the pipeline aborted.
   tc_fence_before();
   __syncthreads();
   if (tid == 0 && *abort_flag) atomicExch(a.status, kStatusTimeout);
