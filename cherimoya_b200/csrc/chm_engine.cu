@@ -191,19 +191,22 @@ EncodeTiledFn encode_tiled() {
 // with the matching swizzle (64 or 128 bytes); out-of-range rows read as
 // zero and are not written by stores.
 int make_act_tmap(CUtensorMap* map, const void* base, long long rows, int CP, int elem_bytes,
-                  int box_bytes) {
+                  int box_bytes, int box_rows = 128) {
   EncodeTiledFn fn = encode_tiled();
   if (!fn) return CHM_ERR_CUDA;
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return CHM_ERR_WORKSPACE;
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(CP), static_cast<cuuint64_t>(rows)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(CP) * elem_bytes};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_bytes / elem_bytes), 128u};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_bytes / elem_bytes),
+                             static_cast<cuuint32_t>(box_rows)};
   const cuuint32_t estr[2] = {1u, 1u};
   const CUresult r = fn(map, elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
                         2, const_cast<void*>(base), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        box_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                        box_bytes == 32   ? CU_TENSOR_MAP_SWIZZLE_32B
+                        : box_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                          : CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? CHM_OK : CHM_ERR_CUDA;
 }
@@ -249,20 +252,31 @@ template <typename act_t>
 int launch_mlp(const Dims& m, const MlpArgs& a, int grid, cudaStream_t st) {
   const bool fast = (m.mode == CHM_MODE_BF16);
   if (m.CP == ws::kC && m.HP == ws::kH) {
-    const int smem = ws::kAlloc;
     MlpMaps tmap;
-    CHM_TRY(make_act_tmap(&tmap.stage, a.X_in, a.rows, m.CP, sizeof(act_t), ws::kBoxBytes));
+    // bf16 residual: the input tile is read and the output tile written by TMA
     CHM_TRY(make_act_tmap(&tmap.res, a.X_in, a.rows, m.CP, sizeof(act_t), 128));
     CHM_TRY(make_act_tmap(&tmap.out, a.X_out, a.rows, m.CP, sizeof(act_t), 128));
     LaunchTimer timer(kKMlp, st);
-    if (fast) {
-      auto k = mlp_ws_kernel<act_t, true>;
+    auto go = [&](auto k, int smem) {
       cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       k<<<grid, ws::kThreads, smem, st>>>(a, tmap);
-    } else {
-      auto k = mlp_ws_kernel<act_t, false>;
-      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      k<<<grid, ws::kThreads, smem, st>>>(a, tmap);
+    };
+    bool wide = false;
+    if constexpr (sizeof(act_t) == 2) {
+      if (fast && a.dil <= ws::kWideMaxDil) {
+        // small dilation: one (128 + 2d)-row block per 64-channel step
+        using Lay = ws::Layout<act_t, true>;
+        CHM_TRY(make_act_tmap(&tmap.stage, a.X_in, a.rows, m.CP, sizeof(act_t),
+                              Lay::kBoxBytes, ws::wide_rows(a.dil)));
+        go(mlp_ws_kernel<act_t, true, true>, Lay::kAlloc);
+        wide = true;
+      }
+    }
+    if (!wide) {
+      using Lay = ws::Layout<act_t, false>;
+      CHM_TRY(make_act_tmap(&tmap.stage, a.X_in, a.rows, m.CP, sizeof(act_t), Lay::kBoxBytes));
+      if (fast) go(mlp_ws_kernel<act_t, true, false>, Lay::kAlloc);
+      else go(mlp_ws_kernel<act_t, false, false>, Lay::kAlloc);
     }
     return launch_status();
   }

@@ -1153,38 +1153,66 @@ constexpr int kResidualWarp0 = kProducerWarps + kEpilogueWarps; // 12
 constexpr int kMmaWarp = kResidualWarp0 + kResidualWarps;       // 16
 constexpr int kTmaWarp = kMmaWarp + 1;                          // 17
 constexpr int kThreads = (kTmaWarp + 1) * 32;                   // 576
-constexpr uint32_t kBoxBytes = 64;                              // staging box row width
-constexpr uint32_t kBox = kBoxBytes * 128;                      // 8 KB staging box
 constexpr uint32_t kResBox = 128 * 128;                         // 16 KB residual box
 constexpr uint32_t kW1 = 0;                                     // 256 x 128 bf16
 constexpr uint32_t kW2 = kW1 + kH * kC * 2;                     // 128 x 256 bf16
-constexpr uint32_t kStg = kW2 + kC * kH * 2;                    // 2 slots x 3 boxes
-constexpr uint32_t kSlotBytes = 3 * kBox;
-constexpr uint32_t kRes = kStg + 2 * kSlotBytes;                // 2 boxes (bf16 tile)
-constexpr uint32_t kConvW = kRes + 2 * kResBox;                 // 3 x 128 fp32
-constexpr uint32_t kBars = kConvW + 3 * kC * 4;
-enum Bar { STG_FULL0, STG_FULL1, STG_EMPTY0, STG_EMPTY1, A1_FULL0, A1_FULL1, A1_EMPTY0,
-           A1_EMPTY1, D1A_FULL, D1B_FULL, A2A_FULL, A2B_FULL, D2_FULL, RES_FULL, RES_DONE,
-           D2_EMPTY, kNumBars };
-constexpr uint32_t kSlot = kBars + kNumBars * 8;
-constexpr uint32_t kAbort = kSlot + 4;
-constexpr uint32_t kBytes = kAbort + 4;
-constexpr uint32_t kAlloc = kBytes + 1024;
+constexpr uint32_t kStg = kW2 + kC * kH * 2;                    // staging ring
+constexpr int kMaxSlots = 5;
+enum Bar : int { STG_FULL0 = 0, STG_EMPTY0 = kMaxSlots, A1_FULL0 = 2 * kMaxSlots, A1_FULL1,
+                 A1_EMPTY0, A1_EMPTY1, D1A_FULL, D1B_FULL, A2A_FULL, A2B_FULL, D2_FULL,
+                 RES_FULL, RES_DONE, D2_EMPTY, kNumBars };
+// Staging ring. Split mode (any dilation): a box step covers kBoxBytes of
+// channels and a slot holds its three 128-row blocks (rows - d, rows,
+// rows + d), 64-byte rows with the 64-byte swizzle. Wide mode (bf16, d <= 64):
+// a box step covers 64 channels and a slot holds ONE block of rows
+// [t0 - d, t0 + 128 + d) with 128-byte rows and the 128-byte swizzle, which
+// contains all three shifted windows: (128 + 2d) row requests per step
+// instead of 3 x 128, and a third of the bytes for small d.
+template <typename act_t, bool kWide>
+struct Layout {
+  static constexpr uint32_t kBoxBytes = kWide ? 128 : 64;
+  static constexpr int kSlots = 2;
+  static constexpr uint32_t kBox = kBoxBytes * 128;               // one 128-row block
+  static constexpr uint32_t kSlotBytes = kWide ? 256 * 128 : 3 * kBox;
+  static constexpr uint32_t kRes = kStg + kSlots * kSlotBytes;   // 2 boxes (bf16 tile)
+  static constexpr uint32_t kConvW = kRes + 2 * kResBox;          // 3 x 128 fp32
+  static constexpr uint32_t kBars = kConvW + 3 * kC * 4;
+  static constexpr uint32_t kSlot = kBars + kNumBars * 8;
+  static constexpr uint32_t kAbort = kSlot + 4;
+  static constexpr uint32_t kAlloc = kAbort + 4 + 1024;
+  static_assert(kSlots <= kMaxSlots, "staging ring depth");
+  static_assert(kAlloc <= 232448, "shared memory per block");
+  static_assert(!kWide || sizeof(act_t) == 2, "wide staging is for bf16 activations");
+  // 16-byte chunk q of staging row r (swizzle on address bits 7.. of the box)
+  __device__ static __forceinline__ uint32_t chunk(int q, int r) {
+    return static_cast<uint32_t>(kWide ? (q ^ (r & 7)) : (q ^ ((r >> 1) & 3)));
+  }
+};
+constexpr int kWideMaxDil = 64;
+// rows of a wide staging block: 128 + 2d rounded up to whole 8-row swizzle
+// atoms (at most 256, the TMA box limit)
+__host__ __device__ constexpr int wide_rows(int dil) { return (kTileRows + 2 * dil + 7) & ~7; }
 constexpr uint32_t kD2Col = 256, kA1Col = 384;
 // TMEM column of the packed bf16 A2 for K-step s (16 h values) of a half
 __host__ __device__ constexpr uint32_t a2_col(int s) { return s < 4 ? 8 * s : 64 + 8 * (s - 4); }
 }  // namespace ws
 
 struct MlpMaps {
-  CUtensorMap stage;   // X_in, 64-byte x 128-row boxes, 64-byte swizzle
+  CUtensorMap stage;   // X_in, staging boxes (Layout::kBoxBytes wide, swizzled)
   CUtensorMap res;     // X_in, 128-byte x 128-row boxes, 128-byte swizzle (bf16 residual)
   CUtensorMap out;     // X_out, same boxes as `res`
 };
 
-template <typename act_t, bool kFastGelu>
+template <typename act_t, bool kFastGelu, bool kWide>
 __global__ void __launch_bounds__(ws::kThreads, 1)
     mlp_ws_kernel(MlpArgs a, const __grid_constant__ MlpMaps maps) {
   using namespace ws;
+  using Lay = Layout<act_t, kWide>;
+  constexpr uint32_t kBoxBytes = Lay::kBoxBytes, kBox = Lay::kBox, kSlotBytes = Lay::kSlotBytes;
+  constexpr uint32_t kRes = Lay::kRes, kConvW = Lay::kConvW, kBars = Lay::kBars;
+  constexpr uint32_t kSlot = Lay::kSlot, kAbort = Lay::kAbort;
+  constexpr int kSlots = Lay::kSlots;
+  constexpr int kCPR = kBoxBytes / 16;                 // 16-byte chunks per staging row
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -1196,16 +1224,21 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
   const act_t* Xi = static_cast<const act_t*>(a.X_in);
   act_t* Xo = static_cast<act_t*>(a.X_out);
   constexpr bool kTmaResidual = sizeof(act_t) == 2;
-  constexpr int kBoxCh = kBoxBytes / sizeof(act_t);             // channels per staging box
+  constexpr int kBoxCh = kBoxBytes / sizeof(act_t);             // channels per box step
   constexpr int kBoxes = kC / kBoxCh;                           // box steps per tile
 
   if (warp == kMmaWarp) tmem_alloc(slot, 512);
   if (tid == 0) {
-    const uint32_t counts[kNumBars] = {1, 1, kProducerWarps * 32, kProducerWarps * 32,
-                                       kProducerWarps * 32, kProducerWarps * 32, 1, 1, 1, 1,
-                                       kEpilogueWarps * 32, kEpilogueWarps * 32, 1, 1,
-                                       kResidualWarps * 32, kResidualWarps * 32};
-    for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], counts[i]);
+    for (int i = 0; i < kNumBars; ++i) {
+      uint32_t count = 1;
+      if ((i >= STG_EMPTY0 && i < STG_EMPTY0 + kMaxSlots) || i == A1_FULL0 || i == A1_FULL1)
+        count = kProducerWarps * 32;
+      else if (i == A2A_FULL || i == A2B_FULL)
+        count = kEpilogueWarps * 32;
+      else if (i == RES_DONE || i == D2_EMPTY)
+        count = kResidualWarps * 32;
+      mbar_init(&bars[i], count);
+    }
     *abort_flag = 0;
     mbar_init_fence();
   }
@@ -1247,7 +1280,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
     const int quarter = warp & 3;                 // TMEM lane quarter = tile rows
     const int rl = quarter * 32 + lane;           // tile row of this thread
     const uint32_t lane_sel = static_cast<uint32_t>(quarter * 32) << 16;
-    uint32_t k = 0;
+    uint32_t slotk = 0, phase = 0;   // box step k -> slot k % kSlots, parity (k / kSlots) & 1
     bool ok = true;
     // statistics of this thread's row in tile `it`, loaded one tile ahead
     auto row_stats = [&](int it2, int& l2) -> float2 {
@@ -1284,31 +1317,82 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       const uint32_t shift_b =
           pack_bf16x2(-kA1Scale * st.x * st.y, -kA1Scale * st.x * st.y);
       const bool hasL = rv && (l - a.dil >= 0), hasR = rv && (l + a.dil < a.L);
-      for (int b = 0; b < kBoxes; ++b, ++k) {
-        const int slotk = k & 1;
-        ok = mbar_wait_abortable(&bars[STG_FULL0 + slotk], (k >> 1) & 1, abort_flag);
+      for (int b = 0; b < kBoxes; ++b) {
+        ok = mbar_wait_abortable(&bars[STG_FULL0 + slotk], phase, abort_flag);
         if (!ok) break;
         if (b == 0) {
           ok = mbar_wait_abortable(&bars[A1_EMPTY0 + buf], ((it >> 1) & 1) ^ 1, abort_flag);
           if (!ok) break;
           tc_fence_after();
         }
-        // conv + LayerNorm of this thread's row over the box's channels; the
-        // box rows are 64 bytes with the 64-byte swizzle (16-byte chunk q of
-        // row r at chunk q ^ ((r >> 1) & 3))
+        // conv + LayerNorm of this thread's row over the box's channels (the
+        // box rows are kBoxBytes wide and swizzled, Layout::chunk)
+        const int cbase = b * kBoxCh;              // first channel of the box step
+        if constexpr (kWide) {
+          // rows rl, rl + d, rl + 2d of the slot's block are this thread's
+          // x[l - d], x[l], x[l + d]; two passes of 32 channels
+          const uint8_t* blk = smem + kStg + slotk * kSlotBytes;
+          const uint32_t* cw2 = reinterpret_cast<const uint32_t*>(smem + kConvW);
+          const int rm = rl, rc = rl + a.dil, rp = rl + 2 * a.dil;
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            uint4 sl[4], sc[4], sr[4];
+#pragma unroll
+            for (int qq = 0; qq < 4; ++qq) {
+              const int q = half * 4 + qq;
+              sl[qq] = *reinterpret_cast<const uint4*>(blk + rm * 128 + Lay::chunk(q, rm) * 16);
+              sc[qq] = *reinterpret_cast<const uint4*>(blk + rc * 128 + Lay::chunk(q, rc) * 16);
+              sr[qq] = *reinterpret_cast<const uint4*>(blk + rp * 128 + Lay::chunk(q, rp) * 16);
+            }
+            if (half == 1) {
+              // the step is in registers: release the slot (proxy fence:
+              // generic reads before the TMA overwrites it)
+              fence_async_smem();
+              mbar_arrive(&bars[STG_EMPTY0 + slotk]);
+            }
+            uint32_t packed[16];
+#pragma unroll
+            for (int qq = 0; qq < 4; ++qq) {
+              const uint4 vl = hasL ? sl[qq] : make_uint4(0, 0, 0, 0);
+              const uint4 vc = sc[qq];
+              const uint4 vr = hasR ? sr[qq] : make_uint4(0, 0, 0, 0);
+              const int pr = (cbase + half * 32 + qq * 8) / 2;
+              const uint4 w0 = *reinterpret_cast<const uint4*>(cw2 + pr);
+              const uint4 w1 = *reinterpret_cast<const uint4*>(cw2 + kC / 2 + pr);
+              const uint4 w2 = *reinterpret_cast<const uint4*>(cw2 + kC + pr);
+              const uint32_t* pl = &vl.x;
+              const uint32_t* pc = &vc.x;
+              const uint32_t* pq = &vr.x;
+              const uint32_t* p0 = &w0.x;
+              const uint32_t* p1 = &w1.x;
+              const uint32_t* p2 = &w2.x;
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                uint32_t y = bf2_mul(p2[e], pq[e]);
+                y = bf2_fma(p1[e], pc[e], y);
+                y = bf2_fma(p0[e], pl[e], y);
+                packed[qq * 4 + e] = bf2_fma(y, scale_b, shift_b);
+              }
+            }
+            if (!rv) {
+#pragma unroll
+              for (int e = 0; e < 16; ++e) packed[e] = 0u;
+            }
+            tmem_st16(tmem + lane_sel + kA1Col + buf * 64 + (cbase + half * 32) / 2, packed);
+          }
+        } else {
         const uint8_t* bL = smem + kStg + (slotk * 3 + 0) * kBox + rl * kBoxBytes;
         const uint8_t* bC = bL + kBox;
         const uint8_t* bR = bL + 2 * kBox;
-        const int cbase = b * kBoxCh;              // first channel of the box
         uint32_t packed[kBoxCh / 2];
         if constexpr (sizeof(act_t) == 2) {
           // bf16x2 conv + LayerNorm: y = w0 xl + w1 xc + w2 xr, a = y rstd - mean rstd,
           // four packed operations per channel pair, no unpacking
           const uint32_t* cw2 = reinterpret_cast<const uint32_t*>(smem + kConvW);
-          uint4 sl[4], sc[4], sr[4];
+          uint4 sl[kCPR], sc[kCPR], sr[kCPR];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint32_t off = static_cast<uint32_t>((q ^ ((rl >> 1) & 3)) * 16);
+          for (int q = 0; q < kCPR; ++q) {
+            const uint32_t off = Lay::chunk(q, rl) * 16;
             sl[q] = *reinterpret_cast<const uint4*>(bL + off);
             sc[q] = *reinterpret_cast<const uint4*>(bC + off);
             sr[q] = *reinterpret_cast<const uint4*>(bR + off);
@@ -1319,7 +1403,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
           fence_async_smem();
           mbar_arrive(&bars[STG_EMPTY0 + slotk]);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
+          for (int q = 0; q < kCPR; ++q) {
             const uint4 vl = hasL ? sl[q] : make_uint4(0, 0, 0, 0);
             const uint4 vc = sc[q];
             const uint4 vr = hasR ? sr[q] : make_uint4(0, 0, 0, 0);
@@ -1343,8 +1427,8 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
           }
         } else {
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {              // 16-byte chunks of the row
-          const uint32_t off = static_cast<uint32_t>((q ^ ((rl >> 1) & 3)) * 16);
+        for (int q = 0; q < kCPR; ++q) {           // 16-byte chunks of the row
+          const uint32_t off = Lay::chunk(q, rl) * 16;
           uint4 vl = *reinterpret_cast<const uint4*>(bL + off);
           const uint4 vc = *reinterpret_cast<const uint4*>(bC + off);
           uint4 vr = *reinterpret_cast<const uint4*>(bR + off);
@@ -1392,6 +1476,11 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
           tmem_st16(col, packed);
         } else {
           tmem_st8(col, packed);
+        }
+        }
+        if (++slotk == static_cast<uint32_t>(kSlots)) {
+          slotk = 0;
+          phase ^= 1u;
         }
         if (!ok) break;
       }
@@ -1621,28 +1710,39 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
   } else {
     // ------------------------------------------------------------ TMA warp
     if (lane == 0 && n_my > 0) {
-      // staging box step k -> (tile k / kBoxes, box k % kBoxes) into slot k & 1
-      auto issue = [&](uint32_t k) {
+      // staging box step k -> (tile k / kBoxes, box k % kBoxes) into slot k % kSlots
+      auto issue = [&](uint32_t k, uint32_t slotk) {
         const int tit = static_cast<int>(k / kBoxes);
         const int b = static_cast<int>(k % kBoxes);
-        const int slotk = k & 1;
         const int y0 = (first + tit * stride) * kTileRows;
-        mbar_expect_tx(&bars[STG_FULL0 + slotk], kSlotBytes);
+        if constexpr (kWide) {
+          // one block of rows [y0 - d, y0 - d + wide_rows(d)) (the map's box)
+          mbar_expect_tx(&bars[STG_FULL0 + slotk], wide_rows(a.dil) * kBoxBytes);
+          tma_load_2d(smem + kStg + slotk * kSlotBytes, &maps.stage, b * kBoxCh, y0 - a.dil,
+                      &bars[STG_FULL0 + slotk]);
+        } else {
+          mbar_expect_tx(&bars[STG_FULL0 + slotk], kSlotBytes);
 #pragma unroll
-        for (int blk = 0; blk < 3; ++blk)
-          tma_load_2d(smem + kStg + (slotk * 3 + blk) * kBox, &maps.stage, b * kBoxCh,
-                      y0 + (blk - 1) * a.dil, &bars[STG_FULL0 + slotk]);
+          for (int blk = 0; blk < 3; ++blk)
+            tma_load_2d(smem + kStg + (slotk * 3 + blk) * kBox, &maps.stage, b * kBoxCh,
+                        y0 + (blk - 1) * a.dil, &bars[STG_FULL0 + slotk]);
+        }
       };
       const uint32_t n_steps = static_cast<uint32_t>(n_my) * kBoxes;
-      issue(0);
-      if (n_steps > 1) issue(1);
-      uint32_t k_next = 2;                 // next staging box step to issue
+      uint32_t k_next = 0;
+      for (; k_next < n_steps && k_next < static_cast<uint32_t>(kSlots); ++k_next)
+        issue(k_next, k_next);
+      uint32_t eslot = 0, ephase = 0;      // slot / parity of the next refill's STG_EMPTY
       const uint64_t t0 = global_ns();
       uint64_t last_progress = t0;
       for (uint32_t spin = 0; k_next < n_steps; ++spin) {
-        if (mbar_try(smem_u32(&bars[STG_EMPTY0 + (k_next & 1)]), ((k_next - 2) >> 1) & 1)) {
-          issue(k_next);
+        if (mbar_try(smem_u32(&bars[STG_EMPTY0 + eslot]), ephase)) {
+          issue(k_next, eslot);
           ++k_next;
+          if (++eslot == static_cast<uint32_t>(kSlots)) {
+            eslot = 0;
+            ephase ^= 1u;
+          }
           last_progress = global_ns();
         } else if ((spin & 255u) == 255u) {
           if (*abort_flag || global_ns() - last_progress > kWaitNs) {
