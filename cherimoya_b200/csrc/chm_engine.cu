@@ -187,29 +187,6 @@ EncodeTiledFn encode_tiled() {
   return fn;
 }
 
-// Activation matrix (rows, CP) as a 2-D tensor of box_bytes x 128-row boxes
-// with the matching swizzle (64 or 128 bytes); out-of-range rows read as
-// zero and are not written by stores.
-int make_act_tmap(CUtensorMap* map, const void* base, long long rows, int CP, int elem_bytes,
-                  int box_bytes, int box_rows = 128) {
-  EncodeTiledFn fn = encode_tiled();
-  if (!fn) return CHM_ERR_CUDA;
-  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return CHM_ERR_WORKSPACE;
-  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(CP), static_cast<cuuint64_t>(rows)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(CP) * elem_bytes};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_bytes / elem_bytes),
-                             static_cast<cuuint32_t>(box_rows)};
-  const cuuint32_t estr[2] = {1u, 1u};
-  const CUresult r = fn(map, elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                             : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
-                        2, const_cast<void*>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        box_bytes == 32   ? CU_TENSOR_MAP_SWIZZLE_32B
-                        : box_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
-                                          : CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? CHM_OK : CHM_ERR_CUDA;
-}
 
 // Activations as a 3-D tensor (channels, L, batch) of 128-byte x 128-row x 1
 // boxes with the 128-byte swizzle: rows outside [0, L) of an example read as
@@ -228,6 +205,32 @@ int make_act_tmap3(CUtensorMap* map, const void* base, int batch, int L, int CP)
                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? CHM_OK : CHM_ERR_CUDA;
+}
+
+// Activations as a 3-D tensor (channels, L, batch) with boxes of box_bytes of
+// channels x box_rows positions x 1 example, swizzle = box width (32, 64 or
+// 128 bytes); positions outside [0, L) read as zero and are not written.
+int make_act_tmap3_box(CUtensorMap* map, const void* base, int batch, int L, int CP,
+                       int elem_bytes, int box_bytes, int box_rows) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn) return CHM_ERR_CUDA;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return CHM_ERR_WORKSPACE;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(CP), static_cast<cuuint64_t>(L),
+                              static_cast<cuuint64_t>(batch)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(CP) * elem_bytes,
+                                 static_cast<cuuint64_t>(CP) * elem_bytes * L};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(box_bytes / elem_bytes),
+                             static_cast<cuuint32_t>(box_rows), 1u};
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  const CUresult r = fn(map, elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                             : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                        3, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        box_bytes == 32   ? CU_TENSOR_MAP_SWIZZLE_32B
+                        : box_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                          : CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? CHM_OK : CHM_ERR_CUDA;
 }
 
@@ -252,29 +255,38 @@ template <typename act_t>
 int launch_mlp(const Dims& m, const MlpArgs& a, int grid, cudaStream_t st) {
   const bool fast = (m.mode == CHM_MODE_BF16);
   if (m.CP == ws::kC && m.HP == ws::kH) {
+    // per-example tiles (the last tile of an example is partial)
+    const int batch = static_cast<int>(a.rows / m.L);
+    MlpArgs ae = a;
+    ae.tpe = (m.L + kTileRows - 1) / kTileRows;
+    ae.n_tiles = batch * ae.tpe;
+    const int egrid = std::max(1, std::min(ae.n_tiles, device_sms()));
     MlpMaps tmap;
     // bf16 residual: the input tile is read and the output tile written by TMA
-    CHM_TRY(make_act_tmap(&tmap.res, a.X_in, a.rows, m.CP, sizeof(act_t), 128));
-    CHM_TRY(make_act_tmap(&tmap.out, a.X_out, a.rows, m.CP, sizeof(act_t), 128));
+    CHM_TRY(make_act_tmap3_box(&tmap.res, a.X_in, batch, m.L, m.CP, sizeof(act_t), 128,
+                               kTileRows));
+    CHM_TRY(make_act_tmap3_box(&tmap.out, a.X_out, batch, m.L, m.CP, sizeof(act_t), 128,
+                               kTileRows));
     LaunchTimer timer(kKMlp, st);
     auto go = [&](auto k, int smem) {
       cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      k<<<grid, ws::kThreads, smem, st>>>(a, tmap);
+      k<<<egrid, ws::kThreads, smem, st>>>(ae, tmap);
     };
     bool wide = false;
     if constexpr (sizeof(act_t) == 2) {
       if (fast && a.dil <= ws::kWideMaxDil) {
         // small dilation: one (128 + 2d)-row block per 64-channel step
         using Lay = ws::Layout<act_t, true>;
-        CHM_TRY(make_act_tmap(&tmap.stage, a.X_in, a.rows, m.CP, sizeof(act_t),
-                              Lay::kBoxBytes, ws::wide_rows(a.dil)));
+        CHM_TRY(make_act_tmap3_box(&tmap.stage, a.X_in, batch, m.L, m.CP, sizeof(act_t),
+                                   Lay::kBoxBytes, ws::wide_rows(a.dil)));
         go(mlp_ws_kernel<act_t, true, true>, Lay::kAlloc);
         wide = true;
       }
     }
     if (!wide) {
       using Lay = ws::Layout<act_t, false>;
-      CHM_TRY(make_act_tmap(&tmap.stage, a.X_in, a.rows, m.CP, sizeof(act_t), Lay::kBoxBytes));
+      CHM_TRY(make_act_tmap3_box(&tmap.stage, a.X_in, batch, m.L, m.CP, sizeof(act_t),
+                                 Lay::kBoxBytes, kTileRows));
       if (fast) go(mlp_ws_kernel<act_t, true, false>, Lay::kAlloc);
       else go(mlp_ws_kernel<act_t, false, false>, Lay::kAlloc);
     }

@@ -304,7 +304,7 @@ __global__ void __launch_bounds__(sm::kThreads) stem_mma_kernel(StemInput in,
   uint8_t* sA = sB + 2 * CP * kK * 2;                 // [kASplits] 128 x 128
   uint64_t* bar = reinterpret_cast<uint64_t*>(sA + kASplits * kTileRows * kK * 2);
   uint32_t* slot = reinterpret_cast<uint32_t*>(bar + 1);
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x, warp = tid >> 5;
   if (warp == 0) tmem_alloc(slot, 256);
   if (tid == 0) {
     mbar_init(bar, 1);
@@ -923,7 +923,8 @@ struct MlpArgs {
   int L;
   int C;
   long long rows;        // B * L
-  int n_tiles;
+  int n_tiles;           // flattened 128-row tiles; per-example tiles in mlp_ws_kernel
+  int tpe;               // mlp_ws_kernel: 128-row tiles per example (ceil(L / 128))
   int* status;
 };
 
@@ -1282,32 +1283,14 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
     const uint32_t lane_sel = static_cast<uint32_t>(quarter * 32) << 16;
     uint32_t slotk = 0, phase = 0;   // box step k -> slot k % kSlots, parity (k / kSlots) & 1
     bool ok = true;
-    // statistics of this thread's row in tile `it`, loaded one tile ahead
-    auto row_stats = [&](int it2, int& l2) -> float2 {
-      const long long r2 = (long long)(first + it2 * stride) * kTileRows + rl;
-      l2 = 0;
-      if (it2 >= n_my || r2 >= a.rows) return make_float2(0.f, 0.f);
-      int n2;
-      if (a.rows < (1LL << 31)) {
-        const uint32_t u = static_cast<uint32_t>(r2);
-        n2 = static_cast<int>(u / static_cast<uint32_t>(a.L));
-        l2 = static_cast<int>(u - static_cast<uint32_t>(n2) * static_cast<uint32_t>(a.L));
-      } else {
-        n2 = static_cast<int>(r2 / a.L);
-        l2 = static_cast<int>(r2 - (long long)n2 * a.L);
-      }
-      return a.stats[n2];
-    };
-    int l_next;
-    float2 st_next = row_stats(0, l_next);
+    // tiles are per example: tile -> (example n, first position l0); rows
+    // outside [0, L) of the example arrive as zero from the 3-D tensor map,
+    // which is the conv's zero padding, so no row needs a mask
+    float2 st_next = (n_my > 0) ? a.stats[first / a.tpe] : make_float2(0.f, 0.f);
     for (int it = 0; it < n_my && ok; ++it) {
       const int buf = it & 1;
-      const long long row0 = (long long)(first + it * stride) * kTileRows;
-      const long long r = row0 + rl;
-      const bool rv = r < a.rows;
-      const int l = l_next;
-      const float2 st = st_next;
-      st_next = row_stats(it + 1, l_next);
+      const float2 st = st_next;                   // statistics loaded one tile ahead
+      if (it + 1 < n_my) st_next = a.stats[(first + (it + 1) * stride) / a.tpe];
       const f2 scale2{st.y, st.y};
       const f2 shift2{-st.x * st.y, -st.x * st.y};
       // bf16 fast path: A1 carries a factor 1/2 (exact), which the GELU of
@@ -1316,7 +1299,6 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       const uint32_t scale_b = pack_bf16x2(kA1Scale * st.y, kA1Scale * st.y);
       const uint32_t shift_b =
           pack_bf16x2(-kA1Scale * st.x * st.y, -kA1Scale * st.x * st.y);
-      const bool hasL = rv && (l - a.dil >= 0), hasR = rv && (l + a.dil < a.L);
       for (int b = 0; b < kBoxes; ++b) {
         ok = mbar_wait_abortable(&bars[STG_FULL0 + slotk], phase, abort_flag);
         if (!ok) break;
@@ -1353,9 +1335,9 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
             uint32_t packed[16];
 #pragma unroll
             for (int qq = 0; qq < 4; ++qq) {
-              const uint4 vl = hasL ? sl[qq] : make_uint4(0, 0, 0, 0);
+              const uint4 vl = sl[qq];
               const uint4 vc = sc[qq];
-              const uint4 vr = hasR ? sr[qq] : make_uint4(0, 0, 0, 0);
+              const uint4 vr = sr[qq];
               const int pr = (cbase + half * 32 + qq * 8) / 2;
               const uint4 w0 = *reinterpret_cast<const uint4*>(cw2 + pr);
               const uint4 w1 = *reinterpret_cast<const uint4*>(cw2 + kC / 2 + pr);
@@ -1373,10 +1355,6 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
                 y = bf2_fma(p0[e], pl[e], y);
                 packed[qq * 4 + e] = bf2_fma(y, scale_b, shift_b);
               }
-            }
-            if (!rv) {
-#pragma unroll
-              for (int e = 0; e < 16; ++e) packed[e] = 0u;
             }
             tmem_st16(tmem + lane_sel + kA1Col + buf * 64 + (cbase + half * 32) / 2, packed);
           }
@@ -1404,9 +1382,9 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
           mbar_arrive(&bars[STG_EMPTY0 + slotk]);
 #pragma unroll
           for (int q = 0; q < kCPR; ++q) {
-            const uint4 vl = hasL ? sl[q] : make_uint4(0, 0, 0, 0);
+            const uint4 vl = sl[q];
             const uint4 vc = sc[q];
-            const uint4 vr = hasR ? sr[q] : make_uint4(0, 0, 0, 0);
+            const uint4 vr = sr[q];
             const int pr = (cbase + q * 8) / 2;    // first channel pair of the chunk
             const uint4 w0 = *reinterpret_cast<const uint4*>(cw2 + pr);
             const uint4 w1 = *reinterpret_cast<const uint4*>(cw2 + kC / 2 + pr);
@@ -1429,11 +1407,9 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
 #pragma unroll
         for (int q = 0; q < kCPR; ++q) {           // 16-byte chunks of the row
           const uint32_t off = Lay::chunk(q, rl) * 16;
-          uint4 vl = *reinterpret_cast<const uint4*>(bL + off);
+          const uint4 vl = *reinterpret_cast<const uint4*>(bL + off);
           const uint4 vc = *reinterpret_cast<const uint4*>(bC + off);
-          uint4 vr = *reinterpret_cast<const uint4*>(bR + off);
-          if (!hasL) vl = make_uint4(0, 0, 0, 0);
-          if (!hasR) vr = make_uint4(0, 0, 0, 0);
+          const uint4 vr = *reinterpret_cast<const uint4*>(bR + off);
           constexpr int kE = 16 / sizeof(act_t);  // elements per chunk
           float fl[kE], fc[kE], fr[kE];
           unpack_chunk<act_t>(vl, fl);
@@ -1457,10 +1433,6 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
             packed[(q * kE + e) / 2 + 1] = pack_bf16x2(y1.x, y1.y);
           }
         }
-        }
-        if (!rv) {
-#pragma unroll
-          for (int e = 0; e < kBoxCh / 2; ++e) packed[e] = 0u;
         }
         if constexpr (sizeof(act_t) != 2) {
           // staging consumed: release the slot (the TMA warp refills it with
@@ -1494,8 +1466,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
     const int ew = warp - kProducerWarps;          // 0..7
     const int quarter = warp & 3;                  // TMEM lane quarter of this warp
     const int g = ew >> 2;                         // warpgroup: half columns [64g, 64g+64)
-    const int rl = quarter * 32 + lane;            // tile row of this thread
-    const uint32_t lane_sel = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t lane_sel = static_cast<uint32_t>(quarter * 32) << 16;   // rows of this warp
     for (int it = 0; it < n_my; ++it) {
       bool ok = true;
 #pragma unroll 1
@@ -1544,10 +1515,11 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
         // after the previous tile's store left the buffer)
         const bool leader = (warp == kResidualWarp0 && lane == 0);
         auto load_res = [&](int tit) {
-          const int y0 = (first + tit * stride) * kTileRows;
+          const int tile = first + tit * stride;
+          const int n = tile / a.tpe, l0 = (tile - n * a.tpe) * kTileRows;
           mbar_expect_tx(&bars[RES_FULL], 2 * kResBox);
-          tma_load_2d(sRes, &maps.res, 0, y0, &bars[RES_FULL]);
-          tma_load_2d(sRes + kResBox, &maps.res, 64, y0, &bars[RES_FULL]);
+          tma_load_3d(sRes, &maps.res, 0, l0, n, &bars[RES_FULL]);
+          tma_load_3d(sRes + kResBox, &maps.res, 64, l0, n, &bars[RES_FULL]);
         };
         if (it == 0 && leader) load_res(0);
         if (!mbar_wait_abortable(&bars[RES_FULL], it & 1, abort_flag)) break;
@@ -1582,9 +1554,10 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
         mbar_arrive(&bars[RES_DONE]);
         if (leader) {
           if (!mbar_wait_abortable(&bars[RES_DONE], it & 1, abort_flag)) break;
-          const int y0 = (first + it * stride) * kTileRows;
-          tma_store_2d(&maps.out, sRes, 0, y0);
-          tma_store_2d(&maps.out, sRes + kResBox, 64, y0);
+          const int tile = first + it * stride;
+          const int n = tile / a.tpe, l0 = (tile - n * a.tpe) * kTileRows;
+          tma_store_3d(&maps.out, sRes, 0, l0, n);        // rows past L are clipped
+          tma_store_3d(&maps.out, sRes + kResBox, 64, l0, n);
           bulk_commit();
           if (it + 1 < n_my) {
             bulk_wait_read0();                            // the tile buffer is free again
@@ -1595,8 +1568,10 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
         }
       } else {
         // residual of D2 on rows read directly from global memory (fp32)
-        const long long r = (long long)(first + it * stride) * kTileRows + rl;
-        const bool rv = r < a.rows;
+        const int tile = first + it * stride;
+        const int n = tile / a.tpe, l = (tile - n * a.tpe) * kTileRows + rl;
+        const bool rv = l < a.L;
+        const long long r = (long long)n * a.L + l;
         constexpr int kVE = 16 / sizeof(act_t);
         constexpr int kPre = 32 / kVE;
         if (!mbar_wait_abortable(&bars[D2_FULL], it & 1, abort_flag)) break;
@@ -1714,18 +1689,19 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       auto issue = [&](uint32_t k, uint32_t slotk) {
         const int tit = static_cast<int>(k / kBoxes);
         const int b = static_cast<int>(k % kBoxes);
-        const int y0 = (first + tit * stride) * kTileRows;
+        const int tile = first + tit * stride;
+        const int n = tile / a.tpe, l0 = (tile - n * a.tpe) * kTileRows;
         if constexpr (kWide) {
-          // one block of rows [y0 - d, y0 - d + wide_rows(d)) (the map's box)
+          // one block of rows [l0 - d, l0 - d + wide_rows(d)) (the map's box)
           mbar_expect_tx(&bars[STG_FULL0 + slotk], wide_rows(a.dil) * kBoxBytes);
-          tma_load_2d(smem + kStg + slotk * kSlotBytes, &maps.stage, b * kBoxCh, y0 - a.dil,
+          tma_load_3d(smem + kStg + slotk * kSlotBytes, &maps.stage, b * kBoxCh, l0 - a.dil, n,
                       &bars[STG_FULL0 + slotk]);
         } else {
           mbar_expect_tx(&bars[STG_FULL0 + slotk], kSlotBytes);
 #pragma unroll
           for (int blk = 0; blk < 3; ++blk)
-            tma_load_2d(smem + kStg + (slotk * 3 + blk) * kBox, &maps.stage, b * kBoxCh,
-                        y0 + (blk - 1) * a.dil, &bars[STG_FULL0 + slotk]);
+            tma_load_3d(smem + kStg + (slotk * 3 + blk) * kBox, &maps.stage, b * kBoxCh,
+                        l0 + (blk - 1) * a.dil, n, &bars[STG_FULL0 + slotk]);
         }
       };
       const uint32_t n_steps = static_cast<uint32_t>(n_my) * kBoxes;
