@@ -449,14 +449,16 @@ int run_forward_t(const Dims& m, const PackLayout& pl, const uint8_t* packed, in
   h.logcounts = logcounts;
   h.L = m.L; h.C = m.C; h.CP = m.CP; h.CPH = cph; h.n_ctl = m.n_ctl; h.n_out = m.n_out;
   h.n_groups = m.n_groups; h.T = m.T; h.Lout = m.Lout;
-  if (sizeof(act_t) == 2 && m.n_ctl == 0 && m.CP == 128 && cph == 128) {
+  h.batch = batch;
+  if (sizeof(act_t) == 2 && m.n_ctl == 0 && m.CP == 128 && cph == 128 &&
+      m.n_groups <= hd3::kMaxGroups) {
     CUtensorMap tmap;
     CHM_TRY(make_act_tmap3(&tmap, xa, batch, m.L, m.CP));
-    cudaFuncSetAttribute(head_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         hd2::kAlloc);
-    dim3 hgrid(m.n_out, batch);
+    cudaFuncSetAttribute(head_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         hd3::kAlloc);
+    const int hgrid = std::max(1, std::min(batch * m.n_out, device_sms()));
     LaunchTimer timer(kKProfile, st);
-    head_tma_kernel<<<hgrid, hd2::kThreads, hd2::kAlloc, st>>>(h, tmap);
+    head_fused_kernel<<<hgrid, hd3::kThreads, hd3::kAlloc, st>>>(h, tmap);
     CHM_TRY(launch_status());
   } else if (!(cph == 256 && split_a)) {
     const int smem = head_smem_bytes(cph, split_a ? 2 : 1);
@@ -743,8 +745,10 @@ int32_t chm_pack_weights(const chm_model_desc* desc, const chm_params* p, void* 
   CHM_TRY(copy(p->fconv_bias, pl.head_fb, m.n_out));
   {
     const long long n = (long long)m.n_out * hd::kNP * head_cph(m);
+    const bool count_rows = (m.n_ctl == 0 && m.n_groups <= hd3::kMaxGroups);
     pack_head_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
-        p->fconv_weight, m.n_out, (int)cin, kHeadTaps, hd::kNP, head_cph(m), dst + pl.head_pk);
+        p->fconv_weight, m.n_out, (int)cin, kHeadTaps, hd::kNP, head_cph(m),
+        count_rows ? p->linear_weight : nullptr, m.n_groups, dst + pl.head_pk);
     CHM_TRY(launch_status());
   }
   CHM_TRY(copy(p->linear_weight, pl.head_lw,

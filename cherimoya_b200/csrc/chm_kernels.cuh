@@ -1897,6 +1897,7 @@ struct HeadArgs {
   float* profile;         // (B, n_out, Lout)
   float* logcounts;       // (B, n_groups)
   int L, C, CP, CPH, n_ctl, n_out, n_groups, T, Lout;
+  int batch;              // head_fused_kernel: examples
 };
 
 __host__ __device__ constexpr uint32_t head_smem_bytes(int CPH, int a_splits) {
@@ -2103,161 +2104,215 @@ __global__ void __launch_bounds__(hd::kThreads) head_kernel(HeadArgs a) {
   }
 }
 
-// Profile + count head for bf16 activations without control tracks: the
+// Profile + count head for bf16 activations without control tracks (C <= 128):
+// persistent, one CTA per SM looping over (output, example) work items. The
 // window tiles come straight from HBM by TMA (3-D tensor map, 128-byte
-// swizzle, two boxes of 64 channels = the K-major operand layout the MMA
-// reads), so no thread touches the A operand; rows outside [0, L) arrive as
-// zero, the profile conv's padding. A is double-buffered and the TMA runs two
-// tiles ahead. Same arithmetic and fixed-order reductions as head_kernel.
-namespace hd2 {
-constexpr int kThreads = 128;
-constexpr uint32_t kBox = 128 * 128;                     // 16 KB
+// swizzle: two boxes of 64 channels = the K-major operand layout the MMA
+// reads), three tiles in flight; rows outside [0, L) arrive as zero, the
+// profile conv's padding. Z = X F^T goes to one of two TMEM buffers. The
+// count head rides in the same MMA: the five spare operand rows after the 75
+// taps hold the count Linear's weights (output 0 only), so Z[w, 75 + g] =
+// sum_c X[w, c] lw[g, c] and logcount[g] = lbias[g] + sum_w Z[w, 75 + g] / Lout
+// over the trimmed window. Diagonal sums of the profile are split over two
+// threads per output and combined in a fixed order (deterministic).
+namespace hd3 {
+constexpr int kThreads = 256;
+constexpr int kABufs = 3;
+constexpr int kMaxGroups = hd::kNP - kHeadTaps;          // 5 spare operand rows
+constexpr uint32_t kBox = 128 * 128;                     // 16 KB: 64 channels x 128 rows
 constexpr uint32_t kB = 0;                               // F hi | lo: 2 x 80 x 128 bf16
-constexpr uint32_t kA = kB + 2 * hd::kNP * 128 * 2;      // 2 buffers x 2 boxes
-constexpr uint32_t kRingOff = kA + 4 * kBox;
-constexpr uint32_t kRed = kRingOff + hd::kRing * hd::kZStride * 4;
-constexpr uint32_t kBars = kRed + 512 * 4;
-constexpr uint32_t kSlot = kBars + 4 * 8;
+constexpr uint32_t kA = 40960;                           // kABufs x 2 boxes
+constexpr uint32_t kRingOff = kA + kABufs * 2 * kBox;
+constexpr uint32_t kPart = kRingOff + hd::kRing * hd::kZStride * 4;
+constexpr uint32_t kRed = kPart + 2 * 128 * 4;
+constexpr uint32_t kBars = kRed + 8 * kMaxGroups * 4 + 32;
+constexpr uint32_t kSlot = kBars + (kABufs + 2) * 8;
 constexpr uint32_t kAlloc = kSlot + 16 + 1024;
-}  // namespace hd2
+static_assert(kA % 1024 == 0 && 2 * hd::kNP * 128 * 2 <= kA, "operand layout");
+static_assert(kAlloc <= 232448, "shared memory per block");
+}  // namespace hd3
 
-__global__ void __launch_bounds__(hd2::kThreads) head_tma_kernel(
+__global__ void __launch_bounds__(hd3::kThreads, 1) head_fused_kernel(
     HeadArgs a, const __grid_constant__ CUtensorMap tmap) {
   using namespace hd;
-  using hd2::kBox;
+  using hd3::kBox;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   constexpr int CPH = 128;
-  uint8_t* sB = smem + hd2::kB;
-  uint8_t* sA = smem + hd2::kA;
-  float* ring = reinterpret_cast<float*>(smem + hd2::kRingOff);
-  float* red = reinterpret_cast<float*>(smem + hd2::kRed);
-  uint64_t* a_full = reinterpret_cast<uint64_t*>(smem + hd2::kBars);     // [2]
-  uint64_t* z_full = a_full + 2;                                          // [2]
-  uint32_t* slot = reinterpret_cast<uint32_t*>(smem + hd2::kSlot);
-  const int o = blockIdx.x, b = blockIdx.y;
+  uint8_t* sB = smem + hd3::kB;
+  uint8_t* sA = smem + hd3::kA;
+  float* ring = reinterpret_cast<float*>(smem + hd3::kRingOff);
+  float* part = reinterpret_cast<float*>(smem + hd3::kPart);      // [2][128]
+  float* red = reinterpret_cast<float*>(smem + hd3::kRed);        // [8 warps][groups]
+  uint64_t* a_full = reinterpret_cast<uint64_t*>(smem + hd3::kBars);   // [kABufs]
+  uint64_t* z_full = a_full + hd3::kABufs;                              // [2]
+  uint32_t* slot = reinterpret_cast<uint32_t*>(smem + hd3::kSlot);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const bool counts = (o == 0);
-  const int W = a.Lout + kHeadTaps - 1;
+  const int W = a.Lout + kHeadTaps - 1;                 // window rows per example
   const int n_tiles = (W + kTileRows - 1) / kTileRows;
-  const int p0 = a.T - kHeadPad;
+  const int p0 = a.T - kHeadPad;                        // first window position
+  const int n_items = a.n_out * a.batch;
+  const int n_mine = (n_items > (int)blockIdx.x)
+                         ? (n_items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x
+                         : 0;
+  const int total = n_mine * n_tiles;                   // this CTA's tile sequence
 
   if (warp == 0) tmem_alloc(slot, 256);
   if (tid == 0) {
-    for (int i = 0; i < 4; ++i) mbar_init(&a_full[i], 1);
+    for (int i = 0; i < hd3::kABufs + 2; ++i) mbar_init(&a_full[i], 1);
     mbar_init_fence();
   }
-  {
-    const uint4* g = reinterpret_cast<const uint4*>(a.fb + (size_t)o * 2 * kNP * CPH * 2);
-    uint4* d = reinterpret_cast<uint4*>(sB);
-    for (int i = tid; i < 2 * kNP * CPH * 2 / 16; i += blockDim.x) d[i] = g[i];
-  }
-  fence_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *slot;
-  auto load = [&](int k) {
-    const int buf = k & 1;
+  auto item_of = [&](int g, int& b, int& o, int& k) {
+    const int i = g / n_tiles;
+    k = g - i * n_tiles;
+    const int item = (int)blockIdx.x + i * (int)gridDim.x;
+    o = item / a.batch;
+    b = item - o * a.batch;
+  };
+  auto load = [&](int g) {
+    int b, o, k;
+    item_of(g, b, o, k);
+    const int buf = g % hd3::kABufs;
     mbar_expect_tx(&a_full[buf], 2 * kBox);
     tma_load_3d(sA + buf * 2 * kBox, &tmap, 0, p0 + k * kTileRows, b, &a_full[buf]);
     tma_load_3d(sA + buf * 2 * kBox + kBox, &tmap, 64, p0 + k * kTileRows, b, &a_full[buf]);
   };
   if (tid == 0) {
-    load(0);
-    if (n_tiles > 1) load(1);
+    if (total > 0) load(0);
+    if (total > 1) load(1);
   }
   const uint32_t sA_addr = smem_u32(sA), sB_addr = smem_u32(sB);
   const uint32_t idesc = idesc_bf16(kTileRows, kNP);
-  const uint32_t lane_sel = static_cast<uint32_t>(warp * 32) << 16;
-  float csum = 0.f;                      // this thread's channel (tid) over [T, L - T)
+  const int rq = warp & 3;                              // TMEM lane quarter
+  const uint32_t lane_sel = static_cast<uint32_t>(rq * 32) << 16;
+  const int w = rq * 32 + lane;                         // tile row of this thread (Z pass)
+  int cur_o = -1;
+  float cnt[hd3::kMaxGroups];
+#pragma unroll
+  for (int gi = 0; gi < hd3::kMaxGroups; ++gi) cnt[gi] = 0.f;
   bool ok = true;
-  for (int k = 0; k < n_tiles; ++k) {
-    const int buf = k & 1;
-    ok = mbar_wait(&a_full[buf], (k >> 1) & 1);
-    if (__syncthreads_or(!ok)) break;
-    if (tid == 0) {
+  for (int g = 0; g < total; ++g) {
+    int b, o, k;
+    item_of(g, b, o, k);
+    if (o != cur_o) {
+      // operand F (hi | lo) of output o; every MMA reading the previous one
+      // has completed (each tile's Z was waited for)
+      const uint4* src = reinterpret_cast<const uint4*>(a.fb + (size_t)o * 2 * kNP * CPH * 2);
+      uint4* dst = reinterpret_cast<uint4*>(sB);
+      for (int i = tid; i < 2 * kNP * CPH * 2 / 16; i += blockDim.x) dst[i] = src[i];
+      fence_async_smem();
+      tc_fence_before();
+      __syncthreads();
       tc_fence_after();
-      uint32_t acc = 0;
-      for (int term = 0; term < 2; ++term) {          // F hi, F lo
-        for (int kk = 0; kk < CPH / 16; ++kk) {
-          const uint64_t da = desc_sw128(sA_addr + buf * 2 * kBox + (kk >> 2) * kBox +
-                                         (kk & 3) * 32);
-          const uint64_t db = desc_sw128(sB_addr + term * (kNP * CPH * 2) +
-                                         (kk >> 2) * (kNP * 128) + (kk & 3) * 32);
-          mma_bf16(tmem + buf * 128, da, db, idesc, acc);
-          acc = 1;
-        }
-      }
-      mma_commit(&z_full[buf]);
+      cur_o = o;
     }
-    if (counts && tid < a.C) {
-      // channel tid over the tile's rows whose position lies in [T, L - T)
-      const int c = tid;
-      const uint8_t* base = sA + buf * 2 * kBox + (c >> 6) * kBox + (c & 7) * 2;
-      const int chunk = (c & 63) >> 3;
-      const int w0 = k * kTileRows;
-      for (int r = 0; r < kTileRows; ++r) {
-        const int p = p0 + w0 + r;
-        if (p >= a.T && p < a.L - a.T && w0 + r < W) {
-          const __nv_bfloat16 v =
-              *reinterpret_cast<const __nv_bfloat16*>(base + r * 128 + ((chunk ^ (r & 7)) * 16));
-          csum += __bfloat162float(v);
+    const int buf = g % hd3::kABufs, zb = g & 1;
+    if (tid == 0) {
+      // A[(g + 2) % 3] was read by the MMA of tile g - 1, complete (waited below)
+      if (g + 2 < total) load(g + 2);
+      ok = mbar_wait(&a_full[buf], (g / hd3::kABufs) & 1);
+      if (ok) {
+        tc_fence_after();
+        uint32_t acc = 0;
+        for (int term = 0; term < 2; ++term) {          // F hi, F lo
+#pragma unroll
+          for (int kk = 0; kk < CPH / 16; ++kk) {
+            const uint64_t da = desc_sw128(sA_addr + buf * 2 * kBox + (kk >> 2) * kBox +
+                                           (kk & 3) * 32);
+            const uint64_t db = desc_sw128(sB_addr + term * (kNP * CPH * 2) +
+                                           (kk >> 2) * (kNP * 128) + (kk & 3) * 32);
+            mma_bf16(tmem + zb * 128, da, db, idesc, acc);
+            acc = 1;
+          }
         }
+        mma_commit(&z_full[zb]);
       }
     }
-    ok = mbar_wait(&z_full[buf], (k >> 1) & 1);
-    fence_async_smem();                 // generic reads of A[buf] before the refill
+    if (__syncthreads_or(!ok)) break;
+    ok = mbar_wait(&z_full[zb], (g >> 1) & 1);
     if (__syncthreads_or(!ok)) break;
     tc_fence_after();
-    if (tid == 0 && k + 2 < n_tiles) load(k + 2);
-    // ---- Z tile -> ring rows (128k + row) mod kRing (columns 0..74)
+    // ---- Z tile -> ring rows (128 k + w) mod kRing; count columns 75..79
     {
-      const int rr = warp * 32 + lane;
-      float* zrow = ring + ((k * kTileRows + rr) % kRing) * kZStride;
+      float* zrow = ring + ((k * kTileRows + w) % kRing) * kZStride;
+      uint32_t r[32];
+      if (warp < 4) {
 #pragma unroll 1
-      for (int part = 0; part < 3; ++part) {
-        const int col = part == 0 ? 0 : (part == 1 ? 32 : 48);   // 48..79 overlaps 32..63
-        uint32_t r[32];
-        tmem_ld32(tmem + buf * 128 + lane_sel + col, r);
+        for (int part_c = 0; part_c < 2; ++part_c) {
+          tmem_ld32(tmem + zb * 128 + lane_sel + part_c * 32, r);
 #pragma unroll
-        for (int qq = 0; qq < 32; ++qq) {
-          const int t = col + qq;
-          if ((part < 2 || t >= 64) && t < kHeadTaps) zrow[t] = __uint_as_float(r[qq]);
+          for (int q = 0; q < 32; ++q) zrow[part_c * 32 + q] = __uint_as_float(r[q]);
+        }
+      } else {
+        tmem_ld32(tmem + zb * 128 + lane_sel + 48, r);   // columns 48..79
+#pragma unroll
+        for (int q = 16; q < 32; ++q) {
+          const int t = 48 + q;
+          if (t < kHeadTaps) zrow[t] = __uint_as_float(r[q]);
+        }
+        const int wr = k * kTileRows + w;                // window row
+        if (o == 0 && wr >= kHeadPad && wr < kHeadPad + a.Lout) {
+#pragma unroll
+          for (int gi = 0; gi < hd3::kMaxGroups; ++gi)
+            cnt[gi] += __uint_as_float(r[kHeadTaps - 48 + gi]);
         }
       }
     }
     tc_fence_before();
     __syncthreads();
+    // ---- diagonal sums: output j = sum_t ring[(j + t) mod kRing][t], two halves
     const int j_lo = (k == 0) ? 0 : k * kTileRows - (kHeadTaps - 1);
     const int j_hi = (k == n_tiles - 1) ? a.Lout
                                         : min(a.Lout, k * kTileRows + kTileRows - (kHeadTaps - 1));
-    for (int j = j_lo + tid; j < j_hi; j += blockDim.x) {
-      float acc = 0.f;
-      int rrow = j % kRing;
-#pragma unroll 5
-      for (int t = 0; t < kHeadTaps; ++t) {
-        acc += ring[rrow * kZStride + t];
-        rrow = (rrow + 1 == kRing) ? 0 : rrow + 1;
+    {
+      const int jj = tid & 127, half = tid >> 7;
+      const int j = j_lo + jj;
+      if (j < j_hi) {
+        const int t0 = half ? 38 : 0, t1 = half ? kHeadTaps : 38;
+        int rrow = (j + t0) % kRing;
+        float acc = 0.f;
+#pragma unroll 4
+        for (int t = t0; t < t1; ++t) {
+          acc += ring[rrow * kZStride + t];
+          rrow = (rrow + 1 == kRing) ? 0 : rrow + 1;
+        }
+        part[half * 128 + jj] = acc;
       }
-      a.profile[((long long)b * a.n_out + o) * a.Lout + j] = acc + a.fbias[o];
     }
     __syncthreads();
+    if (tid < 128) {
+      const int j = j_lo + tid;
+      if (j < j_hi)
+        a.profile[((long long)b * a.n_out + o) * a.Lout + j] =
+            (part[tid] + part[128 + tid]) + a.fbias[o];
+    }
+    // ---- count head at the end of an item of output 0: fixed-order reduction
+    if (o == 0 && k == n_tiles - 1) {
+      if (warp >= 4) {
+#pragma unroll
+        for (int gi = 0; gi < hd3::kMaxGroups; ++gi) {
+          float v = cnt[gi];
+#pragma unroll
+          for (int sh = 16; sh > 0; sh >>= 1) v += __shfl_xor_sync(0xffffffffu, v, sh);
+          if (lane == 0) red[(warp - 4) * hd3::kMaxGroups + gi] = v;
+          cnt[gi] = 0.f;
+        }
+      }
+      __syncthreads();
+      if (tid < a.n_groups) {
+        const float s4 = ((red[tid] + red[hd3::kMaxGroups + tid]) +
+                          red[2 * hd3::kMaxGroups + tid]) + red[3 * hd3::kMaxGroups + tid];
+        a.logcounts[(long long)b * a.n_groups + tid] =
+            a.lbias[tid] + s4 / static_cast<float>(a.Lout);
+      }
+    }
   }
   if (!ok && tid == 0) atomicExch(a.status, kStatusTimeout);
-  if (counts && ok) {
-    red[tid] = (tid < a.C) ? csum / static_cast<float>(a.Lout) : 0.f;
-    __syncthreads();
-    const int cin = a.C;
-    for (int g = warp; g < a.n_groups; g += blockDim.x / 32) {
-      float v = 0.f;
-      for (int c = lane; c < a.C; c += 32) v += a.lw[(long long)g * cin + c] * red[c];
-#pragma unroll
-      for (int sh = 16; sh > 0; sh >>= 1) v += __shfl_xor_sync(0xffffffffu, v, sh);
-      if (lane == 0) a.logcounts[(long long)b * a.n_groups + g] = a.lbias[g] + v;
-    }
-  }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -2450,14 +2505,20 @@ __global__ void pack_sw128_split_kernel(const float* __restrict__ src, int R, in
 
 // Profile-head weight F (n_out, Cin, 75) -> per output o a transposed
 // [taps x channels] operand, hi and lo: dst[o] = [hi | lo], each NP x CPH.
+// When lw is given (no control tracks, n_groups <= NP - taps), the spare rows
+// taps .. taps + n_groups - 1 of output 0 hold the count Linear's weights
+// lw[g, c], so the same MMA produces sum_c X[w, c] lw[g, c].
 __global__ void pack_head_kernel(const float* __restrict__ F, int n_out, int Cin, int taps,
-                                 int NP, int CPH, uint8_t* __restrict__ dst) {
+                                 int NP, int CPH, const float* __restrict__ lw, int n_groups,
+                                 uint8_t* __restrict__ dst) {
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (long long)n_out * NP * CPH) return;
   const int o = static_cast<int>(i / ((long long)NP * CPH));
   const int rem = static_cast<int>(i - (long long)o * NP * CPH);
   const int t = rem / CPH, c = rem - (rem / CPH) * CPH;
-  const float v = (t < taps && c < Cin) ? F[((long long)o * Cin + c) * taps + t] : 0.f;
+  float v = (t < taps && c < Cin) ? F[((long long)o * Cin + c) * taps + t] : 0.f;
+  if (lw != nullptr && o == 0 && t >= taps && t - taps < n_groups && c < Cin)
+    v = lw[(long long)(t - taps) * Cin + c];
   const __nv_bfloat16 h = __float2bfloat16_rn(v);
   uint8_t* base = dst + (size_t)o * 2 * NP * CPH * 2;
   const uint32_t off = sw128_offset(t, c, NP);
