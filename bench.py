@@ -36,6 +36,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "seqs/sec fwd (2114bp, 9-layer) & ISM mutants/sec at 1/2/4/8 B200; % roofline"
+MLP_DRAM_BYTES_PER_SEQ = (138.728704e6 + 94.934528e6) / 256   # measured, bf16 mode
 L = 2114
 C, H, N_LAYERS = 128, 256, 9
 # algorithmic work per sequence of the default model (one track)
@@ -329,7 +330,12 @@ def run_ours(args, world, rank, local):
         "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
         "peak_source": "{} bf16_tflops_sustained".format(peak_src),
         "frac_of_burst": achieved / peaks["bf16_tflops"],
-        "traffic": None,
+        # DRAM bytes of one MLP launch: ncu dram__bytes_read.sum + write.sum of the
+        # layer-0 launch at batch 256 (138.73 MB + 94.93 MB, profile committed in
+        # profiles/mlp_ws_kernel_bf16_b256.md), scaled by the sequences processed
+        "traffic": (MLP_DRAM_BYTES_PER_SEQ * args.batch) if args.mode == "bf16" else None,
+        "traffic_unit": "bytes per launch",
+        "algorithmic_bytes": 2.0 * L * C * (2 if args.mode == "bf16" else 4) * args.batch,
         "flop_per_launch": mlp_flop, "avg_launch_ms": mlp_avg_ms,
         "whole_forward_tflops_per_gpu": model_tflops,
         "whole_forward_frac": model_tflops / peak,

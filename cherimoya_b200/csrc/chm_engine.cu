@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <type_traits>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -317,23 +318,40 @@ int launch_stats(const Dims& m, const act_t* X, const float* convw, int dil, int
   (void)counters;
   if constexpr (sizeof(act_t) == 2) {
     // segment length: long segments amortise the two halo rows, short ones
-    // avoid dead slots when the chains are short (large dilation)
+    // avoid dead slots when the chains are short (large dilation); pick the
+    // length with the fewest load slots plus per-segment overhead
     const int K = (m.L + dil - 1) / dil;            // longest chain
-    const int kS = K >= 64 ? 12 : (K >= 12 ? 8 : 4);
+    static const int kLens[] = {4, 6, 8, 9, 12};
+    int kS = 4;
+    long best = -1;
+    for (int len : kLens) {
+      const long nkb = (K + len - 1) / len;
+      const long cost = nkb * (len + 2) + 3 * nkb;
+      if (best < 0 || cost < best) {
+        best = cost;
+        kS = len;
+      }
+    }
     const int n_kb = (K + kS - 1) / kS;
     LaunchTimer timer(kKStats, st);
     auto go = [&](auto kern) {
       kern<<<batch, kStatsChainThreads, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(X), convw,
                                                  dil, m.L, m.C, n_kb, 1e-3f, stats);
     };
+    auto pick = [&](auto cp) {
+      constexpr int CPc = decltype(cp)::value;
+      switch (kS) {
+        case 4: go(stats_chain_kernel<CPc, 4>); break;
+        case 6: go(stats_chain_kernel<CPc, 6>); break;
+        case 8: go(stats_chain_kernel<CPc, 8>); break;
+        case 9: go(stats_chain_kernel<CPc, 9>); break;
+        default: go(stats_chain_kernel<CPc, 12>); break;
+      }
+    };
     if (m.CP == 64) {
-      if (kS == 12) go(stats_chain_kernel<64, 12>);
-      else if (kS == 8) go(stats_chain_kernel<64, 8>);
-      else go(stats_chain_kernel<64, 4>);
+      pick(std::integral_constant<int, 64>{});
     } else if (m.CP == 128) {
-      if (kS == 12) go(stats_chain_kernel<128, 12>);
-      else if (kS == 8) go(stats_chain_kernel<128, 8>);
-      else go(stats_chain_kernel<128, 4>);
+      pick(std::integral_constant<int, 128>{});
     } else {
       return CHM_ERR_UNSUPPORTED;
     }
