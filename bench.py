@@ -331,8 +331,8 @@ def run_ours(args, world, rank, local):
         "peak_source": "{} bf16_tflops_sustained".format(peak_src),
         "frac_of_burst": achieved / peaks["bf16_tflops"],
         # DRAM bytes of one MLP launch: ncu dram__bytes_read.sum + write.sum of the
-        # layer-0 launch at batch 256 (138.73 MB + 94.93 MB, profile committed in
-        # profiles/mlp_ws_kernel_bf16_b256.md), scaled by the sequences processed
+        # layer-0 launch at batch 256 (138.73 MB + 94.93 MB), scaled by the
+        # sequences processed
         "traffic": (MLP_DRAM_BYTES_PER_SEQ * args.batch) if args.mode == "bf16" else None,
         "traffic_unit": "bytes per launch",
         "algorithmic_bytes": 2.0 * L * C * (2 if args.mode == "bf16" else 4) * args.batch,
