@@ -66,6 +66,9 @@ struct LaunchTimer {
 constexpr size_t kAlign = 1024;
 size_t align_up(size_t v, size_t a = kAlign) { return (v + a - 1) / a * a; }
 int round64(int v) { return (v + 63) / 64 * 64; }
+// padded channel width: 64, 128 or 256 (kernels tile channels in 64-wide
+// operand boxes and assume the width divides their thread layouts)
+int pad_channels(int c) { return c <= 64 ? 64 : (c <= 128 ? 128 : round64(c) <= 256 ? 256 : round64(c)); }
 
 struct Dims {
   int C, CP, H, HP, L, T, Lout, n_layers, n_out, n_groups, n_ctl, mode;
@@ -77,7 +80,7 @@ struct Dims {
 Dims dims_of(const chm_model_desc* d) {
   Dims m;
   m.C = d->n_filters;
-  m.CP = round64(d->n_filters);
+  m.CP = pad_channels(d->n_filters);
   m.H = d->expansion * d->n_filters;
   m.HP = round64(m.H);
   m.L = d->seq_len;
@@ -293,6 +296,25 @@ int launch_mlp(const Dims& m, const MlpArgs& a, int grid, cudaStream_t st) {
     }
     return launch_status();
   }
+  if (m.CP == 256 || m.HP > 256) {
+    // wide models: weights streamed chunk by chunk
+    LaunchTimer timer(kKMlp, st);
+    auto go = [&](auto k, int smem) {
+      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      k<<<grid, 256, smem, st>>>(a);
+    };
+    auto pick = [&](auto cp) {
+      constexpr int CPc = decltype(cp)::value;
+      const int smem = static_cast<int>(StreamSmem<CPc>::kAlloc);
+      if (fast) go(mlp_stream_kernel<act_t, CPc, true>, smem);
+      else go(mlp_stream_kernel<act_t, CPc, false>, smem);
+    };
+    if (m.CP == 64) pick(std::integral_constant<int, 64>{});
+    else if (m.CP == 128) pick(std::integral_constant<int, 128>{});
+    else if (m.CP == 256) pick(std::integral_constant<int, 256>{});
+    else return CHM_ERR_UNSUPPORTED;
+    return launch_status();
+  }
   if (m.CP == 64) {
     switch (m.HP) {
       case 64: return launch_mlp_t<act_t, 64, 64>(a, grid, st, fast);
@@ -352,6 +374,8 @@ int launch_stats(const Dims& m, const act_t* X, const float* convw, int dil, int
       pick(std::integral_constant<int, 64>{});
     } else if (m.CP == 128) {
       pick(std::integral_constant<int, 128>{});
+    } else if (m.CP == 256) {
+      pick(std::integral_constant<int, 256>{});
     } else {
       return CHM_ERR_UNSUPPORTED;
     }
@@ -363,6 +387,9 @@ int launch_stats(const Dims& m, const act_t* X, const float* convw, int dil, int
                                                                       1e-3f, stats);
   } else if (m.CP == 128) {
     stats_example_kernel<act_t, 128><<<batch, kStats2Threads, 0, st>>>(X, convw, dil, m.L, m.C,
+                                                                       1e-3f, stats);
+  } else if (m.CP == 256) {
+    stats_example_kernel<act_t, 256><<<batch, kStats2Threads, 0, st>>>(X, convw, dil, m.L, m.C,
                                                                        1e-3f, stats);
   } else {
     return CHM_ERR_UNSUPPORTED;
@@ -448,6 +475,8 @@ int run_forward_t(const Dims& m, const PackLayout& pl, const uint8_t* packed, in
     a.C = m.C;
     a.rows = rows;
     a.n_tiles = n_tiles;
+    a.tpe = 0;
+    a.HP = m.HP;
     a.status = status;
     CHM_TRY(launch_mlp<act_t>(m, a, grid, st));
     std::swap(xa, xb);
@@ -537,7 +566,7 @@ int validate(const chm_model_desc* d) {
   if (d->mode != CHM_MODE_FP32 && d->mode != CHM_MODE_BF16) return CHM_ERR_INVALID_ARGUMENT;
   if (d->seq_len - 2 * d->trimming < 1) return CHM_ERR_UNSUPPORTED;
   const Dims m = dims_of(d);
-  if (m.CP > 128 || m.HP > 256) return CHM_ERR_UNSUPPORTED;
+  if (m.CP > 256 || m.HP > 512) return CHM_ERR_UNSUPPORTED;
   const int cin = m.C + m.n_ctl;
   if (cin > 256) return CHM_ERR_UNSUPPORTED;
   if ((cin * kHeadWin + kHeadWarps * kHeadJ) * 4 > 227 * 1024 && head_cph(m) == 256 &&
@@ -591,7 +620,7 @@ VarLayout var_layout(const Dims& m, int n_pairs) {
 Dims block_dims(int C, int H, int x_dtype) {
   Dims m{};
   m.C = C;
-  m.CP = round64(C);
+  m.CP = pad_channels(C);
   m.H = H;
   m.HP = round64(H);
   m.mode = (x_dtype == CHM_INPUT_BF16) ? CHM_MODE_BF16 : CHM_MODE_FP32;
@@ -600,7 +629,7 @@ Dims block_dims(int C, int H, int x_dtype) {
 }
 
 bool block_supported(int C, int H) {
-  return C >= 1 && H >= C && round64(C) <= 128 && round64(H) <= 256;
+  return C >= 1 && H >= C && pad_channels(C) <= 256 && round64(H) <= 512;
 }
 
 struct BlockWsLayout {
@@ -657,6 +686,8 @@ int run_block_t(const Dims& m, int batch, int dil, const uint8_t* packed, const 
   a.C = m.C;
   a.rows = rows;
   a.n_tiles = n_tiles;
+  a.tpe = 0;
+  a.HP = m.HP;
   a.status = reinterpret_cast<int*>(ws + bl.status);
   CHM_TRY(launch_mlp<act_t>(m, a, std::min(n_tiles, device_sms()), st));
   if (m.C != m.CP) {

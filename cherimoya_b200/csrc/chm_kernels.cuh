@@ -39,7 +39,12 @@ template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(flo
 template <typename T, int N> struct Vec;
 template <int N> struct Vec<float, N> {
   static __device__ __forceinline__ void load(const float* p, float (&v)[N]) {
-    if constexpr (N == 4) {
+    if constexpr (N == 8) {
+      const float4 t = *reinterpret_cast<const float4*>(p);
+      const float4 u = *reinterpret_cast<const float4*>(p + 4);
+      v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+      v[4] = u.x; v[5] = u.y; v[6] = u.z; v[7] = u.w;
+    } else if constexpr (N == 4) {
       float4 t = *reinterpret_cast<const float4*>(p);
       v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
     } else if constexpr (N == 2) {
@@ -63,7 +68,13 @@ template <int N> struct Vec<float, N> {
 };
 template <int N> struct Vec<__nv_bfloat16, N> {
   static __device__ __forceinline__ void load(const __nv_bfloat16* p, float (&v)[N]) {
-    if constexpr (N == 4) {
+    if constexpr (N == 8) {
+      const uint4 t = *reinterpret_cast<const uint4*>(p);
+      v[0] = __uint_as_float(t.x << 16); v[1] = __uint_as_float(t.x & 0xFFFF0000u);
+      v[2] = __uint_as_float(t.y << 16); v[3] = __uint_as_float(t.y & 0xFFFF0000u);
+      v[4] = __uint_as_float(t.z << 16); v[5] = __uint_as_float(t.z & 0xFFFF0000u);
+      v[6] = __uint_as_float(t.w << 16); v[7] = __uint_as_float(t.w & 0xFFFF0000u);
+    } else if constexpr (N == 4) {
       uint2 t = *reinterpret_cast<const uint2*>(p);
       __nv_bfloat162 a = *reinterpret_cast<__nv_bfloat162*>(&t.x);
       __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&t.y);
@@ -925,6 +936,7 @@ struct MlpArgs {
   long long rows;        // B * L
   int n_tiles;           // flattened 128-row tiles; per-example tiles in mlp_ws_kernel
   int tpe;               // mlp_ws_kernel: 128-row tiles per example (ceil(L / 128))
+  int HP;                // mlp_stream_kernel: padded hidden width
   int* status;
 };
 
@@ -1109,6 +1121,229 @@ __global__ void __launch_bounds__(128, 1) mlp_kernel(MlpArgs a) {
     __syncthreads();
   }
   if (failed && tid == 0) atomicExch(a.status, kStatusTimeout);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ============================================================== MLP, streamed weights
+// Cheri Block update for wide models (C up to 256, H up to 512), whose W1 and
+// W2 do not fit in shared memory together. Per 128-row tile (one CTA per SM,
+// persistent, 8 warps):
+//   A1 = bf16((conv(X) - mean) * rstd)      -> shared memory (K-major, swizzled)
+//   for each chunk of 64 hidden units hc:
+//     D1 = A1 * W1[hc]^T                    (tcgen05, TMEM, K = CP)
+//     A2 = bf16(gelu(D1))                   -> shared memory
+//     D2 (+)= A2 * W2[:, hc]^T              (tcgen05, TMEM, K = 64)
+//   X_out = X + D2
+// The weight chunks (W1 rows [64 hc, 64 hc + 64): CP/64 pieces of 8 KB; W2
+// columns of chunk hc: one CP x 128-byte piece, both straight from the packed
+// 128-byte-swizzled layout) stream in by 1-D bulk copies into two buffers, one
+// chunk ahead. Upstream cheri.py:1072-1082.
+template <int CP>
+struct StreamSmem {
+  static constexpr uint32_t kA1 = 0;                          // CP/64 x (128 x 128 B)
+  static constexpr uint32_t kWBuf = static_cast<uint32_t>(CP) * 256;   // W1 chunk + W2 chunk
+  static constexpr uint32_t kW = kA1 + static_cast<uint32_t>(CP) * 256;
+  static constexpr uint32_t kA2 = kW + 2 * kWBuf;             // 128 x 64 bf16
+  static constexpr uint32_t kBars = kA2 + 128 * 128;
+  static constexpr uint32_t kSlot = kBars + 4 * 8;
+  static constexpr uint32_t kAlloc = kSlot + 16 + 1024;
+  static_assert(kAlloc <= 232448, "shared memory per block");
+};
+
+template <typename act_t, int CP, bool kFastGelu>
+__global__ void __launch_bounds__(256, 1) mlp_stream_kernel(MlpArgs a) {
+  static_assert(CP == 64 || CP == 128 || CP == 256, "channel width");
+  using S = StreamSmem<CP>;
+  const int HP = a.HP;                               // padded hidden width, multiple of 64
+  const int kChunks = HP / 64;
+  constexpr int CPL = CP / 32;                       // channels per lane when building A1
+  constexpr uint32_t kTmemCols = (CP + 64 <= 256) ? 256 : 512;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sA1 = smem + S::kA1;
+  uint8_t* sW = smem + S::kW;
+  uint8_t* sA2 = smem + S::kA2;
+  uint64_t* wfull = reinterpret_cast<uint64_t*>(smem + S::kBars);   // [2]
+  uint64_t* mbar = wfull + 2;
+  uint32_t* slot = reinterpret_cast<uint32_t*>(smem + S::kSlot);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const act_t* Xi = static_cast<const act_t*>(a.X_in);
+  act_t* Xo = static_cast<act_t*>(a.X_out);
+
+  if (warp == 0) tmem_alloc(slot, kTmemCols);
+  if (tid == 0) {
+    mbar_init(&wfull[0], 1);
+    mbar_init(&wfull[1], 1);
+    mbar_init(mbar, 1);
+    mbar_init_fence();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *slot;
+  const uint32_t tD2 = tmem;                         // columns [0, CP)
+  const uint32_t tD1 = tmem + CP;                    // columns [CP, CP + 64)
+  const uint32_t lane_sel = static_cast<uint32_t>((warp & 3) * 32) << 16;
+  const uint32_t sA1_addr = smem_u32(sA1), sW_addr = smem_u32(sW), sA2_addr = smem_u32(sA2);
+  constexpr uint32_t kIdesc1 = idesc_bf16(kTileRows, 64);
+  constexpr uint32_t kIdesc2 = idesc_bf16(kTileRows, CP);
+  const int n_my = (a.n_tiles > (int)blockIdx.x)
+                       ? (a.n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x
+                       : 0;
+  const long long total = (long long)n_my * kChunks;   // weight chunks this CTA uses
+  // weight chunk g (hidden chunk g % kChunks) -> buffer g & 1
+  auto load_w = [&](long long g) {
+    const int hc = static_cast<int>(g % kChunks), buf = static_cast<int>(g & 1);
+    uint8_t* dst = sW + buf * S::kWBuf;
+    mbar_expect_tx(&wfull[buf], S::kWBuf);
+#pragma unroll
+    for (int kb = 0; kb < CP / 64; ++kb)
+      bulk_load(dst + kb * 8192, a.w1 + ((size_t)kb * HP + 64 * hc) * 128, 8192, &wfull[buf]);
+    bulk_load(dst + (CP / 64) * 8192, a.w2 + (size_t)hc * CP * 128, CP * 128, &wfull[buf]);
+  };
+  if (tid == 0) {
+    if (total > 0) load_w(0);
+    if (total > 1) load_w(1);
+  }
+  float cw0[CPL], cw1[CPL], cw2[CPL];
+  const int c0 = lane * CPL;
+#pragma unroll
+  for (int j = 0; j < CPL; ++j) {
+    cw0[j] = a.convw[c0 + j];
+    cw1[j] = a.convw[CP + c0 + j];
+    cw2[j] = a.convw[2 * CP + c0 + j];
+  }
+  bool ok = true;
+  uint32_t mph = 0;                                  // MMA barrier completions so far
+  for (int it = 0; it < n_my && ok; ++it) {
+    const long long row0 = (long long)((int)blockIdx.x + it * (int)gridDim.x) * kTileRows;
+    // ---- A1: conv + LayerNorm (warp w builds rows 16w .. 16w + 15)
+    for (int i = 0; i < 16; ++i) {
+      const int rl = warp * 16 + i;
+      const long long r = row0 + rl;
+      float v[CPL];
+#pragma unroll
+      for (int j = 0; j < CPL; ++j) v[j] = 0.f;
+      if (r < a.rows) {
+        const int n = static_cast<int>(r / a.L);
+        const int l = static_cast<int>(r - (long long)n * a.L);
+        const float2 st = a.stats[n];
+        float xc[CPL], xl[CPL], xr[CPL];
+#pragma unroll
+        for (int j = 0; j < CPL; ++j) { xl[j] = 0.f; xr[j] = 0.f; }
+        Vec<act_t, CPL>::load(Xi + r * CP + c0, xc);
+        if (l - a.dil >= 0) Vec<act_t, CPL>::load(Xi + (r - a.dil) * CP + c0, xl);
+        if (l + a.dil < a.L) Vec<act_t, CPL>::load(Xi + (r + a.dil) * CP + c0, xr);
+#pragma unroll
+        for (int j = 0; j < CPL; ++j) {
+          const float y = fmaf(cw0[j], xl[j], fmaf(cw1[j], xc[j], cw2[j] * xr[j]));
+          v[j] = (c0 + j < a.C) ? (y - st.x) * st.y : 0.f;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < CPL; j += 2)
+        *reinterpret_cast<uint32_t*>(sA1 + sw128_offset(rl, c0 + j, kTileRows)) =
+            pack_bf16x2(v[j], v[j + 1]);
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    for (int hc = 0; hc < kChunks && ok; ++hc) {
+      const long long g = (long long)it * kChunks + hc;
+      const int buf = static_cast<int>(g & 1);
+      const uint32_t w1_addr = sW_addr + buf * S::kWBuf;
+      const uint32_t w2_addr = w1_addr + (CP / 64) * 8192;
+      // ---- GEMM1: D1 = A1 * W1[hc]^T
+      if (tid == 0) {
+        ok = mbar_wait(&wfull[buf], static_cast<uint32_t>((g >> 1) & 1));
+        if (ok) {
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < CP / 16; ++k) {
+            const uint64_t da = desc_sw128(sA1_addr + (k >> 2) * (kTileRows * 128) + (k & 3) * 32);
+            const uint64_t db = desc_sw128(w1_addr + (k >> 2) * 8192 + (k & 3) * 32);
+            mma_bf16(tD1, da, db, kIdesc1, k > 0 ? 1u : 0u);
+          }
+          mma_commit(mbar);
+        }
+      }
+      if (__syncthreads_or(!ok)) { ok = false; break; }
+      ok = mbar_wait(mbar, mph & 1);
+      ++mph;
+      if (__syncthreads_or(!ok)) { ok = false; break; }
+      tc_fence_after();
+      // ---- GELU: thread (row, half) -> 32 hidden units -> A2 (bf16, swizzled)
+      {
+        const int rl = (warp & 3) * 32 + lane, half = warp >> 2;
+        uint32_t r[32];
+        tmem_ld32(tD1 + lane_sel + half * 32, r);
+        uint32_t p[16];
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          if constexpr (kFastGelu) {
+            p[q] = gelu_bf16x2(__uint_as_float(r[2 * q]), __uint_as_float(r[2 * q + 1]));
+          } else {
+            p[q] = pack_bf16x2(gelu_tanh<false>(__uint_as_float(r[2 * q])),
+                               gelu_tanh<false>(__uint_as_float(r[2 * q + 1])));
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          *reinterpret_cast<uint4*>(sA2 + sw128_offset(rl, half * 32 + q * 8, kTileRows)) =
+              make_uint4(p[4 * q], p[4 * q + 1], p[4 * q + 2], p[4 * q + 3]);
+      }
+      fence_async_smem();
+      tc_fence_before();
+      __syncthreads();
+      // ---- GEMM2: D2 (+)= A2 * W2[:, hc]^T; then buffer `buf` is free again
+      if (tid == 0) {
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint64_t da = desc_sw128(sA2_addr + (k & 3) * 32);
+          const uint64_t db = desc_sw128(w2_addr + (k & 3) * 32);
+          mma_bf16(tD2, da, db, kIdesc2, (hc > 0 || k > 0) ? 1u : 0u);
+        }
+        mma_commit(mbar);
+      }
+      ok = mbar_wait(mbar, mph & 1);
+      ++mph;
+      if (__syncthreads_or(!ok)) { ok = false; break; }
+      tc_fence_after();
+      if (tid == 0 && g + 2 < total) load_w(g + 2);
+    }
+    if (!ok) break;
+    // ---- residual: X_out = X_in + D2 (thread = row, half of the channels)
+    {
+      const int rl = (warp & 3) * 32 + lane, half = warp >> 2;
+      const long long r = row0 + rl;
+#pragma unroll 1
+      for (int j = 0; j < CP / 64; ++j) {
+        const int cb = half * (CP / 2) + j * 32;
+        uint32_t d[32];
+        tmem_ld32(tD2 + lane_sel + cb, d);
+        if (r < a.rows) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            float x[4];
+            Vec<act_t, 4>::load(Xi + r * CP + cb + q * 4, x);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) x[e] += __uint_as_float(d[q * 4 + e]);
+            Vec<act_t, 4>::store(Xo + r * CP + cb + q * 4, x);
+          }
+        }
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+  }
+  if (!ok && tid == 0) atomicExch(a.status, kStatusTimeout);
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {

@@ -115,6 +115,18 @@ __device__ __forceinline__ void tma_store_2d(const void* tmap, const void* src, 
       "r"(smem_u32(src)), "r"(x), "r"(y)
       : "memory");
 }
+// 1-D bulk copy global -> this CTA's shared memory (no tensor map): `bytes` a
+// multiple of 16, both addresses 16-byte aligned; completes `bytes` of
+// transaction on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // 3-D tiled TMA store (bulk async group); elements outside the tensor are
 // not written.
 __device__ __forceinline__ void tma_store_3d(const void* tmap, const void* src, int x, int y,
