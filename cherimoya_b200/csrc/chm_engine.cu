@@ -424,7 +424,8 @@ int run_forward_t(const Dims& m, const PackLayout& pl, const uint8_t* packed, in
       CUtensorMap tmap;
       CHM_TRY(make_act_tmap3(&tmap, xa, batch, m.L, m.CP));
       const int tiles = batch * ((m.L + kTileRows - 1) / kTileRows);
-      const int tgrid = std::max(1, std::min((tiles + 1) / 2, device_sms()));
+      const int tgrid =
+          std::max(1, std::min((tiles + sm2::kGroups - 1) / sm2::kGroups, device_sms()));
       const int tsmem = static_cast<int>(sm2::smem_bytes(1));
       auto go = [&](auto k) {
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, tsmem);

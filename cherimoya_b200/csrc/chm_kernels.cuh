@@ -435,7 +435,7 @@ __global__ void __launch_bounds__(sm::kThreads) stem_mma_kernel(StemInput in,
 }
 
 // Stem for bf16 activations with C <= 128 (CP = 128): per-example tiles of
-// 128 positions (17 per 2114-bp sequence), two warpgroups per CTA, each with
+// 128 positions (17 per 2114-bp sequence), four warpgroups per CTA, each with
 // its own tile stream, A buffer and TMEM accumulator, so one group's im2col
 // and epilogue overlap the other's. With the tap-major K order an im2col row
 // is a contiguous window of 8-byte input columns (4 channels of one
@@ -446,7 +446,8 @@ __global__ void __launch_bounds__(sm::kThreads) stem_mma_kernel(StemInput in,
 // stores; positions past the end of the sequence are clipped by the tensor
 // map.
 namespace sm2 {
-constexpr int kThreads = 256;
+constexpr int kGroups = 4;                         // warpgroups, one tile stream each
+constexpr int kThreads = 128 * kGroups;
 constexpr int kCols = kTileRows + kStemTaps - 1;   // 148 staged input columns
 constexpr int kKSteps = 6;                         // K = 84 -> 96
 constexpr int kChunks = kKSteps * 2;               // 16-byte chunks written per row
@@ -455,15 +456,19 @@ constexpr uint32_t kA = kTileRows * sm::kK * 2;    // 32 KB
 __host__ __device__ constexpr uint32_t cols_bytes(int a_splits) {
   return static_cast<uint32_t>(a_splits * kCols * 8);
 }
-// [W hi|lo][A group 0][A group 1][cols 0][cols 1][bias][barriers]: every
-// swizzled operand / TMA box starts on a 1024-byte boundary
-__host__ __device__ constexpr uint32_t cols_off(int a_splits) { return kW + 2 * a_splits * kA; }
+// [W hi|lo][A group 0..3][cols 0..3][bias][barriers]: every swizzled operand /
+// TMA box starts on a 1024-byte boundary
+__host__ __device__ constexpr uint32_t cols_off(int a_splits) {
+  return kW + kGroups * a_splits * kA;
+}
 __host__ __device__ constexpr uint32_t cols_stride(int a_splits) {
   return (cols_bytes(a_splits) + 127) & ~127u;
 }
 __host__ __device__ constexpr uint32_t smem_bytes(int a_splits) {
-  return cols_off(a_splits) + 2 * cols_stride(a_splits) + 128 * 4 + 64 + 1024;
+  return cols_off(a_splits) + kGroups * cols_stride(a_splits) + 128 * 4 + 8 * kGroups + 16 +
+         1024;
 }
+static_assert(smem_bytes(1) <= 232448, "shared memory per block");
 static_assert(kW % 1024 == 0 && kA % 1024 == 0, "swizzled buffers need 1024-byte alignment");
 }  // namespace sm2
 
@@ -486,13 +491,13 @@ __global__ void __launch_bounds__(sm2::kThreads, 1) stem_tc_kernel(
   uint8_t* sA = smem + kW + g * kASplits * kA;       // [kASplits] 128 x 128 bf16
   uint2* cols = reinterpret_cast<uint2*>(smem + cols_off(kASplits) +
                                          g * cols_stride(kASplits));   // [kASplits][kCols]
-  float* sbias = reinterpret_cast<float*>(smem + cols_off(kASplits) + 2 * cols_stride(kASplits));
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sbias + 128);    // [2]
-  uint32_t* slot = reinterpret_cast<uint32_t*>(bar + 2);
-  if (warp == 0) tmem_alloc(slot, 256);
+  float* sbias =
+      reinterpret_cast<float*>(smem + cols_off(kASplits) + kGroups * cols_stride(kASplits));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sbias + 128);    // [kGroups]
+  uint32_t* slot = reinterpret_cast<uint32_t*>(bar + kGroups);
+  if (warp == 0) tmem_alloc(slot, 128 * kGroups);
   if (tid == 0) {
-    mbar_init(&bar[0], 1);
-    mbar_init(&bar[1], 1);
+    for (int i = 0; i < kGroups; ++i) mbar_init(&bar[i], 1);
     mbar_init_fence();
   }
   {
@@ -513,7 +518,7 @@ __global__ void __launch_bounds__(sm2::kThreads, 1) stem_tc_kernel(
   const uint32_t bar_id = 1 + g;
   uint32_t it = 0;
   bool ok = true;
-  for (int tile = blockIdx.x * 2 + g; tile < n_tiles; tile += gridDim.x * 2, ++it) {
+  for (int tile = blockIdx.x * kGroups + g; tile < n_tiles; tile += gridDim.x * kGroups, ++it) {
     const int b = tile / tpe;
     const int l0 = (tile - b * tpe) * kTileRows;
     // ---- stage input columns l0 - 10 .. l0 + 137 (zero outside [0, L))
@@ -608,7 +613,7 @@ __global__ void __launch_bounds__(sm2::kThreads, 1) stem_tc_kernel(
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(*slot, 256);
+    tmem_dealloc(*slot, 128 * kGroups);
   }
 }
 
