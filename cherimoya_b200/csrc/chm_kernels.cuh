@@ -232,57 +232,6 @@ __device__ __forceinline__ void stem_column(const StemInput& in, int L, int b, i
   }
 }
 
-// ============================================================== stem
-// X0[b, l, c] = gelu_tanh(bias[c] + sum_{k<4, t<21} W[c, k, t] x[b, k, l + t - 10])
-// (upstream cherimoya.py:173-174, 373). One thread per channel, kStemL
-// consecutive positions; the input window is staged in shared memory.
-constexpr int kStemL = 32;
-
-template <typename act_t, int kIn>
-__global__ void __launch_bounds__(256) stem_kernel(StemInput in, const float* __restrict__ w,
-                                                   const float* __restrict__ bias, act_t* X,
-                                                   int L, int C, int CP) {
-  __shared__ float win[4][kStemL + kStemTaps - 1];
-  const int b = blockIdx.y;
-  const int l0 = blockIdx.x * kStemL;
-  const int c = threadIdx.x;
-  for (int i = threadIdx.x; i < kStemL + kStemTaps - 1; i += blockDim.x) {
-    const int p = l0 + i - kStemPad;
-    float col[4] = {0.f, 0.f, 0.f, 0.f};
-    if (p >= 0 && p < L) stem_column<kIn>(in, L, b, p, col);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) win[k][i] = col[k];
-  }
-  __syncthreads();
-  if (c >= CP) return;
-  float acc[kStemL];
-  const float b0 = (c < C) ? bias[c] : 0.f;
-#pragma unroll
-  for (int i = 0; i < kStemL; ++i) acc[i] = b0;
-  if (c < C) {
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-#pragma unroll
-      for (int t = 0; t < kStemTaps; ++t) {
-        const float wt = w[(c * 4 + k) * kStemTaps + t];
-#pragma unroll
-        for (int i = 0; i < kStemL; ++i) acc[i] = fmaf(wt, win[k][i + t], acc[i]);
-      }
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < kStemL; ++i) {
-    const int l = l0 + i;
-    if (l < L) {
-      const float v = acc[i];
-      const float y = (c < C) ? 0.5f * v * (1.0f + tanhf(0.7978845608028654f *
-                                                          (v + 0.044715f * v * v * v)))
-                              : 0.f;
-      X[((long long)b * L + l) * CP + c] = from_f32<act_t>(y);
-    }
-  }
-}
-
 // ============================================================== stem, tcgen05
 // Stem as an im2col GEMM over 128-row tiles of the flattened (B*L) rows:
 //   A[r, 4t + k] = x[b, k, l + t - 10]  (K = 84 tap-major, padded to 128)
@@ -620,119 +569,10 @@ __global__ void __launch_bounds__(sm2::kThreads, 1) stem_tc_kernel(
 // ============================================================== stats
 // Per-example LayerNorm statistics of the dilated depthwise conv output
 // y = w0 x[l-d] + w1 x[l] + w2 x[l+d] over the (L, C) plane (upstream
-// cheri.py:84-98). Each block reduces kStatsRows rows to (count, mean, M2)
-// with a two-pass in-register reduction; the last block of an example
-// combines the partials in index order (Chan et al.'s pairwise update), so
-// the result is deterministic. Writes stats[b] = (mean, 1/sqrt(var + eps)).
-template <typename act_t, int CP>
-__global__ void __launch_bounds__(256) stats_kernel(const act_t* __restrict__ X,
-                                                    const float* __restrict__ convw, int dil,
-                                                    int L, int C, float eps,
-                                                    float* __restrict__ partials,
-                                                    unsigned int* __restrict__ counters,
-                                                    float2* __restrict__ stats) {
-  constexpr int CPL = CP / 32;             // channels per lane
-  constexpr int kRowsPerWarp = kStatsRows / 8;
-  __shared__ float red[8];
-  __shared__ float s_mean;
-  __shared__ bool s_last;
-  const int b = blockIdx.y;
-  const int chunk = blockIdx.x;
-  const int n_chunks = gridDim.x;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int c0 = lane * CPL;
-  float w0[CPL], w1[CPL], w2[CPL];
-#pragma unroll
-  for (int j = 0; j < CPL; ++j) {
-    w0[j] = convw[c0 + j];
-    w1[j] = convw[CP + c0 + j];
-    w2[j] = convw[2 * CP + c0 + j];
-  }
-  const act_t* Xb = X + (long long)b * L * CP;
-  float y[kRowsPerWarp][CPL];
-  float s = 0.f;
-  const int row_base = chunk * kStatsRows + warp * kRowsPerWarp;
-#pragma unroll
-  for (int i = 0; i < kRowsPerWarp; ++i) {
-    const int l = row_base + i;
-    float xc[CPL], xl[CPL], xr[CPL];
-#pragma unroll
-    for (int j = 0; j < CPL; ++j) { xc[j] = 0.f; xl[j] = 0.f; xr[j] = 0.f; }
-    if (l < L) {
-      Vec<act_t, CPL>::load(Xb + (long long)l * CP + c0, xc);
-      if (l - dil >= 0) Vec<act_t, CPL>::load(Xb + (long long)(l - dil) * CP + c0, xl);
-      if (l + dil < L) Vec<act_t, CPL>::load(Xb + (long long)(l + dil) * CP + c0, xr);
-    }
-#pragma unroll
-    for (int j = 0; j < CPL; ++j) {
-      const float v = fmaf(w0[j], xl[j], fmaf(w1[j], xc[j], w2[j] * xr[j]));
-      y[i][j] = (l < L && c0 + j < C) ? v : 0.f;
-      s += y[i][j];
-    }
-  }
-  const int rows_here = min(kStatsRows, L - chunk * kStatsRows);
-  const float count = static_cast<float>(rows_here) * static_cast<float>(C);
-  // pass 1: chunk mean
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  if (lane == 0) red[warp] = s;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float t = 0.f;
-    for (int i = 0; i < 8; ++i) t += red[i];
-    s_mean = t / count;
-  }
-  __syncthreads();
-  const float mean = s_mean;
-  // pass 2: sum of squared deviations from the chunk mean
-  float q = 0.f;
-#pragma unroll
-  for (int i = 0; i < kRowsPerWarp; ++i) {
-    const int l = row_base + i;
-#pragma unroll
-    for (int j = 0; j < CPL; ++j) {
-      const float dv = y[i][j] - mean;
-      q += (l < L && c0 + j < C) ? dv * dv : 0.f;
-    }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
-  __syncthreads();
-  if (lane == 0) red[warp] = q;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float m2 = 0.f;
-    for (int i = 0; i < 8; ++i) m2 += red[i];
-    float* part = partials + ((long long)b * n_chunks + chunk) * 3;
-    part[0] = count;
-    part[1] = mean;
-    part[2] = m2;
-    __threadfence();
-    const unsigned int prev = atomicAdd(&counters[b], 1u);
-    s_last = (prev == static_cast<unsigned int>(n_chunks - 1));
-  }
-  __syncthreads();
-  if (!s_last || threadIdx.x != 0) return;
-  __threadfence();
-  const volatile float* pb = partials + (long long)b * n_chunks * 3;
-  float na = pb[0], ma = pb[1], qa = pb[2];
-  for (int i = 1; i < n_chunks; ++i) {
-    const float nb = pb[i * 3], mb = pb[i * 3 + 1], qb = pb[i * 3 + 2];
-    const float nab = na + nb;
-    const float delta = mb - ma;
-    ma = ma + delta * (nb / nab);
-    qa = qa + qb + delta * delta * (na * nb / nab);
-    na = nab;
-  }
-  const float var = qa / na;
-  stats[b] = make_float2(ma, 1.0f / sqrtf(var + eps));
-  counters[b] = 0u;  // leave the counter ready for the next layer / call
-}
-
-// Per-example statistics, one block per example (replaces the chunked
-// version for the bandwidth-bound hot path). Lanes read 8 channels (16 B
-// bf16 / 32 B fp32); CP/8 lanes cover one row, so a warp streams 256/CP*...
-// rows per load instruction. Each thread accumulates sum(y) and sum(y^2)
+// cheri.py:84-98), any activation type, one block per example (the fp32
+// path; bf16 activations use stats_chain_kernel below). Lanes read 8
+// channels (16 B bf16 / 32 B fp32); CP/8 lanes cover one row, so a warp
+// covers 256/CP rows per load instruction. Each thread accumulates sum(y) and sum(y^2)
 // of one row's 8 channels in fp32 and adds them into fp64 accumulators; the
 // block reduction is fp64 in a fixed order, so the result is deterministic
 // and var = E[y^2] - mean^2 does not cancel catastrophically.
