@@ -265,26 +265,49 @@ def run_ours(args, world, rank, local):
         dev_ms_max = max_over_ranks(dev_ms, world, dev)
         value = world * args.batch * args.steps / (dev_ms_max / 1000.0)
 
-        # ---- end to end through the public API, host buffers
+        # ---- end to end through the public API, host buffers: every step copies
+        # its one-hot input from pinned host memory and reads its outputs back.
+        # The copy of step k+1's input runs on a second stream while step k
+        # computes (two device input buffers), as a serving loop would.
         e2e = None
         if not args.no_e2e:
             Xh = make_inputs(args.batch, 1 + rank).pin_memory()
             ph = torch.empty((args.batch, 1, L - 2 * model.trimming), dtype=torch.float32,
                              pin_memory=True)
             ch = torch.empty((args.batch, 1), dtype=torch.float32, pin_memory=True)
-            for _ in range(args.warmup):
-                p, c = model(Xh.to(dev, non_blocking=True))
-                ph.copy_(p, non_blocking=True)
-                ch.copy_(c, non_blocking=True)
+            xd = [torch.empty_like(Xh, device=dev) for _ in range(2)]
+            copy_stream = torch.cuda.Stream(device=dev)
+            compute = torch.cuda.current_stream(dev)
+
+            def run_steps(n):
+                copied = [torch.cuda.Event() for _ in range(2)]
+                consumed = [torch.cuda.Event() for _ in range(2)]
+                with torch.cuda.stream(copy_stream):
+                    copy_stream.wait_stream(compute)       # after the start event
+                    xd[0].copy_(Xh, non_blocking=True)
+                    copied[0].record(copy_stream)
+                for k in range(n):
+                    b = k % 2
+                    if k + 1 < n:
+                        nb = (k + 1) % 2
+                        with torch.cuda.stream(copy_stream):
+                            if k >= 1:
+                                copy_stream.wait_event(consumed[nb])
+                            xd[nb].copy_(Xh, non_blocking=True)
+                            copied[nb].record(copy_stream)
+                    compute.wait_event(copied[b])
+                    p, c = model(xd[b])
+                    consumed[b].record(compute)
+                    ph.copy_(p, non_blocking=True)
+                    ch.copy_(c, non_blocking=True)
+
+            run_steps(args.warmup)
             torch.cuda.synchronize()
             barrier(world)
             e_s = torch.cuda.Event(enable_timing=True)
             e_e = torch.cuda.Event(enable_timing=True)
             e_s.record()
-            for _ in range(args.steps):
-                p, c = model(Xh.to(dev, non_blocking=True))
-                ph.copy_(p, non_blocking=True)
-                ch.copy_(c, non_blocking=True)
+            run_steps(args.steps)
             e_e.record()
             torch.cuda.synchronize()
             barrier(world)
@@ -292,7 +315,8 @@ def run_ours(args, world, rank, local):
             e2e = {"value": world * args.batch * args.steps / (e2e_ms / 1000.0),
                    "unit": "seqs/s", "h2d_bytes_per_step": Xh.numel() * Xh.element_size(),
                    "d2h_bytes_per_step": ph.numel() * 4 + ch.numel() * 4,
-                   "api": "Cherimoya.forward(X) on pinned host one-hot fp32 input"}
+                   "api": "Cherimoya.forward(X) on pinned host one-hot fp32 input; the "
+                          "next step's H2D copy overlaps the current step"}
 
         # ---- saturation mutagenesis (sharded by sequence, weak scaling)
         ism = None

@@ -288,3 +288,33 @@ def test_variant_effect_matches_oracle(golden):
     d, j = cb.variant_effect(m, ref.to(DEV), alt.to(DEV))
     assert (d.cpu() - rd).abs().max() <= 2e-6
     assert (j.cpu() - rj).abs().max() <= 2e-6
+
+
+def test_forward_captures_in_cuda_graph(golden):
+    """The engine forward has no host synchronisation or allocation of its
+    own, so a whole model call records into a CUDA graph; replays with new
+    input contents give the eager results."""
+    case = golden("model_default_L2114")
+    m = _model(case, "bf16")
+    X = O.one_hot(case["bases"]).to(DEV)
+    Xs = X.clone()
+    with torch.no_grad():
+        ref_p, ref_c = m(X)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                m(Xs)                                   # warm-up on the side stream
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            gp, gc = m(Xs)
+        Xs.copy_(X.flip(0))
+        g.replay()
+        torch.cuda.synchronize()
+        fp, fc = m(X.flip(0))
+        assert torch.equal(gp, fp) and torch.equal(gc, fc)
+        Xs.copy_(X)
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(gp, ref_p) and torch.equal(gc, ref_c)
