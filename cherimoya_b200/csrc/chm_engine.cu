@@ -771,7 +771,8 @@ int32_t chm_pack_weights(const chm_model_desc* desc, const chm_params* p, void* 
   };
   CHM_TRY(copy(p->iconv_weight, pl.stem_w, (long long)m.C * 4 * kStemTaps));
   pack_sw128_split_kernel<<<(m.CP * sm::kK + 255) / 256, 256, 0, st>>>(
-      p->iconv_weight, m.C, 4 * kStemTaps, m.CP, sm::kK, kStemTaps, dst + pl.stem_pk);
+      p->iconv_weight, m.C, 4 * kStemTaps, m.CP, sm::kK, kStemTaps, p->iconv_bias,
+      dst + pl.stem_pk);
   CHM_TRY(launch_status());
   CHM_TRY(copy(p->iconv_bias, pl.stem_b, m.C));
   for (int i = 0; i < m.n_layers; ++i) {

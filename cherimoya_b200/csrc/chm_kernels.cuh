@@ -494,8 +494,12 @@ __global__ void __launch_bounds__(sm2::kThreads, 1) stem_tc_kernel(
       uint8_t* dst = sA + sp * kA;
 #pragma unroll
       for (int q = 0; q < kChunks; ++q) {
+        // K column 84 (the first after the 21 taps x 4 channels) is the
+        // constant 1 that multiplies the packed bias column of W
+        const uint2 one = (sp == 0 && 2 * q + 1 == kStemTaps) ? make_uint2(0x3F80u, 0u)
+                                                               : make_uint2(0u, 0u);
         const uint2 a = (2 * q < kStemTaps) ? cs[2 * q] : make_uint2(0u, 0u);
-        const uint2 c = (2 * q + 1 < kStemTaps) ? cs[2 * q + 1] : make_uint2(0u, 0u);
+        const uint2 c = (2 * q + 1 < kStemTaps) ? cs[2 * q + 1] : one;
         *reinterpret_cast<uint4*>(dst + sw128_offset(gt, 8 * q, kTileRows)) =
             make_uint4(a.x, a.y, c.x, c.y);
       }
@@ -537,12 +541,10 @@ __global__ void __launch_bounds__(sm2::kThreads, 1) stem_tc_kernel(
         uint32_t pk[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const int c = j * 32 + q * 8 + 2 * e;
-          const float z0 = __uint_as_float(d[q * 8 + 2 * e]) + sbias[c];
-          const float z1 = __uint_as_float(d[q * 8 + 2 * e + 1]) + sbias[c + 1];
-          const float y0 = (c < C) ? gelu_tanh<true>(z0) : 0.f;
-          const float y1 = (c + 1 < C) ? gelu_tanh<true>(z1) : 0.f;
-          pk[e] = pack_bf16x2(y0, y1);
+          // the bias came through the MMA; channels >= C have zero weights
+          // and bias, so GELU(0) = 0 there
+          pk[e] = gelu_bf16x2(__uint_as_float(d[q * 8 + 2 * e]),
+                              __uint_as_float(d[q * 8 + 2 * e + 1]));
         }
         *reinterpret_cast<uint4*>(sA + sw128_offset(gt, j * 32 + q * 8, kTileRows)) =
             make_uint4(pk[0], pk[1], pk[2], pk[3]);
@@ -2565,8 +2567,11 @@ __global__ void pack_sw128_kernel(const float* __restrict__ src, int R, int K, i
 // (lo = value - bf16(value)); dst holds [hi | lo], each RP x KP.
 // taps > 0: src rows are (channels x taps) channel-major and the packed K
 // order is tap-major, k = channels * t + c  <-  src column taps * c + t.
+// extra (optional, length R) fills column K: the stem bias, multiplied by a
+// constant-one A column in the bf16 stem and by a zero column elsewhere.
 __global__ void pack_sw128_split_kernel(const float* __restrict__ src, int R, int K, int RP,
-                                        int KP, int taps, uint8_t* __restrict__ dst) {
+                                        int KP, int taps, const float* __restrict__ extra,
+                                        uint8_t* __restrict__ dst) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= RP * KP) return;
   const int r = i / KP, k = i - (i / KP) * KP;
@@ -2575,7 +2580,8 @@ __global__ void pack_sw128_split_kernel(const float* __restrict__ src, int R, in
     const int chans = K / taps;
     ks = (k % chans) * taps + k / chans;
   }
-  const float v = (r < R && k < K) ? src[(long long)r * K + ks] : 0.f;
+  float v = (r < R && k < K) ? src[(long long)r * K + ks] : 0.f;
+  if (extra != nullptr && k == K && r < R) v = extra[r];
   const __nv_bfloat16 h = __float2bfloat16_rn(v);
   const uint32_t off = sw128_offset(r, k, RP);
   *reinterpret_cast<__nv_bfloat16*>(dst + off) = h;
