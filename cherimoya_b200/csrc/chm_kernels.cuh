@@ -1313,13 +1313,14 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
   if (warp == kMmaWarp) tmem_alloc(slot, 512);
   if (tid == 0) {
     for (int i = 0; i < kNumBars; ++i) {
+      // thread-side barriers count warps (mbar_arrive_warp)
       uint32_t count = 1;
       if ((i >= STG_EMPTY0 && i < STG_EMPTY0 + kMaxSlots) || i == A1_FULL0 || i == A1_FULL1)
-        count = kProducerWarps * 32;
+        count = kProducerWarps;
       else if (i == A2A_FULL || i == A2B_FULL)
-        count = kEpilogueWarps * 32;
+        count = kEpilogueWarps;
       else if (i == RES_DONE || i == D2_EMPTY)
-        count = kResidualWarps * 32;
+        count = kResidualWarps;
       mbar_init(&bars[i], count);
     }
     *abort_flag = 0;
@@ -1412,7 +1413,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
               // the step is in registers: release the slot (proxy fence:
               // generic reads before the TMA overwrites it)
               fence_async_smem();
-              mbar_arrive(&bars[STG_EMPTY0 + slotk]);
+              mbar_arrive_warp(&bars[STG_EMPTY0 + slotk]);
             }
             uint32_t packed[16];
 #pragma unroll
@@ -1461,7 +1462,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
           // overlaps the arithmetic (proxy fence: generic reads before the
           // TMA overwrites the slot)
           fence_async_smem();
-          mbar_arrive(&bars[STG_EMPTY0 + slotk]);
+          mbar_arrive_warp(&bars[STG_EMPTY0 + slotk]);
 #pragma unroll
           for (int q = 0; q < kCPR; ++q) {
             const uint4 vl = sl[q];
@@ -1522,7 +1523,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
           // before the TMA (async proxy) overwrites the slot; without it the
           // refill can land before the reads complete.
           fence_async_smem();
-          mbar_arrive(&bars[STG_EMPTY0 + slotk]);
+          mbar_arrive_warp(&bars[STG_EMPTY0 + slotk]);
         }
         // packed channels [cbase, cbase + kBoxCh) -> A1 columns cbase / 2 ...
         const uint32_t col = tmem + lane_sel + kA1Col + buf * 64 + cbase / 2;
@@ -1541,7 +1542,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       if (!ok) break;
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&bars[A1_FULL0 + buf]);
+      mbar_arrive_warp(&bars[A1_FULL0 + buf]);
     }
   } else if (warp < kResidualWarp0) {
     // ------------------------------------------------------------ GELU epilogue
@@ -1578,7 +1579,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
         }
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(&bars[hh ? A2B_FULL : A2A_FULL]);
+        mbar_arrive_warp(&bars[hh ? A2B_FULL : A2A_FULL]);
       }
       if (!ok) break;
     }
@@ -1619,7 +1620,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
           tmem_ld32(tmem + lane_sel + kD2Col + jj * 32, d);
           if (jj == 3) {
             tc_fence_before();
-            mbar_arrive(&bars[D2_EMPTY]);                 // D2 fully read
+            mbar_arrive_warp(&bars[D2_EMPTY]);            // D2 fully read
           }
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
@@ -1633,7 +1634,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
           }
         }
         fence_async_smem();                               // generic writes -> TMA store
-        mbar_arrive(&bars[RES_DONE]);
+        mbar_arrive_warp(&bars[RES_DONE]);
         if (leader) {
           if (!mbar_wait_abortable(&bars[RES_DONE], it & 1, abort_flag)) break;
           const int tile = first + it * stride;
@@ -1685,7 +1686,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
         }
         }
         tc_fence_before();
-        mbar_arrive(&bars[D2_EMPTY]);
+        mbar_arrive_warp(&bars[D2_EMPTY]);
       }
     }
   } else if (warp == kMmaWarp) {
