@@ -21,6 +21,16 @@ oracle (the upstream PyTorch CPU path restated) on the host cores.
 --impl reference times the upstream algorithm's CPU implementation (the
 oracle port) on the same workload, a bounded sample of sequences per step,
 on rank 0 only.
+
+--workload selects the model and input set (the default is the one above):
+  forward    default 9-layer model, uniform random sequences, batch 1024
+  multitask  the same backbone with 1 unstranded + 4 stranded tracks
+             (signal_groups [1, 2, 2, 2, 2]: 9 profile tracks, 5 count
+             heads), batch 2048, per-sequence GC fraction uniform in
+             [0.35, 0.65]
+  variant    12-layer n_filters 256 model (trimming 557), ref/alt pairs
+             differing by one SNV at the centre position (alt uniform among
+             the 3 other bases), 512 pairs per GPU per step; unit pairs/s
 """
 
 import argparse
@@ -38,12 +48,26 @@ sys.path.insert(0, ROOT)
 METRIC = "seqs/sec fwd (2114bp, 9-layer) & ISM mutants/sec at 1/2/4/8 B200; % roofline"
 MLP_DRAM_BYTES_PER_SEQ = (138.728704e6 + 94.934528e6) / 256   # measured, bf16 mode
 L = 2114
-C, H, N_LAYERS = 128, 256, 9
-# algorithmic work per sequence of the default model (one track)
-MLP_FLOP_PER_SEQ = 4 * C * H * L * N_LAYERS                 # 2,493,775,872
-FLOP_PER_SEQ = MLP_FLOP_PER_SEQ + 2 * 84 * C * L + 6 * C * L * N_LAYERS + 2 * C * 75 * 1000
-IN_BYTES_PER_SEQ = 4 * 4 * L                                  # fp32 one-hot
-OUT_BYTES_PER_SEQ = 4 * (1000 + 1)
+WORKLOADS = {
+    # name: (model kwargs, default batch per GPU, input seed base, unit)
+    "forward": ({}, 1024, 1, "seqs/s"),
+    "multitask": ({"signal_groups": [1, 2, 2, 2, 2]}, 2048, 2, "seqs/s"),
+    "variant": ({"n_filters": 256, "n_layers": 12, "trimming": 557}, 512, 3, "pairs/s"),
+}
+
+
+def flop_per_seq(model):
+    """Algorithmic FLOP of one forward: MLP 4 C H L per layer, stem 2*84 C L,
+    depthwise conv 6 C L per layer, profile head 2 C 75 n_out over the
+    trimmed window (2,573,047,296 for the default model)."""
+    C, H, nl = model.n_filters, model.n_filters * model.expansion, model.n_layers
+    l_out = L - 2 * model.trimming
+    return (4 * C * H * L * nl + 2 * 84 * C * L + 6 * C * L * nl
+            + 2 * C * 75 * model.n_outputs * l_out)
+
+
+def mlp_flop_per_seq(model):
+    return 4 * model.n_filters * model.n_filters * model.expansion * L * model.n_layers
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -149,29 +173,67 @@ def make_inputs(batch, seed):
     return one_hot(torch.randint(0, 4, (batch, L), generator=g))
 
 
-def cpu_forward_rate(n_seqs, min_seconds=10.0, max_reps=8):
-    """Oracle (upstream PyTorch CPU path restated) fp32 forward on the host
-    cores: sequences/s over a bounded sample of n_seqs sequences."""
+def make_bases(workload, batch, seed):
+    """Input bases (0..3 = A, C, G, T) of a workload: a tuple of (batch, L)
+    int64 tensors, one per model input (ref and alt for variant pairs)."""
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    if workload == "multitask":
+        # per-sequence GC fraction gc ~ U(0.35, 0.65); C and G each gc / 2
+        gc = 0.35 + 0.3 * torch.rand(batch, 1, generator=g)
+        u = torch.rand(batch, L, generator=g)
+        bases = torch.where(u < gc / 2, 1, torch.where(u < gc, 2,
+                            torch.where(u < gc + (1 - gc) / 2, 0, 3)))
+        return (bases,)
+    ref = torch.randint(0, 4, (batch, L), generator=g)
+    if workload != "variant":
+        return (ref,)
+    alt = ref.clone()
+    c = L // 2
+    alt[:, c] = (ref[:, c] + torch.randint(1, 4, (batch,), generator=g)) % 4
+    return (ref, alt)
+
+
+def build_model(args):
+    import torch
+    import cherimoya_b200 as cb
+    torch.manual_seed(0)
+    return cb.Cherimoya(compile=False, precision=args.mode, **WORKLOADS[args.workload][0])
+
+
+def oracle_step(args, n):
+    """The oracle's (upstream PyTorch CPU path restated) fp32 work for n units
+    of the workload: a callable running it once."""
     import torch
     from oracle import cherimoya_oracle as O
-    import cherimoya_b200 as cb
+    m = build_model(args)
+    sd = {k: v.detach().float().clone() for k, v in m.state_dict().items()}
+    cfg = m._init_kwargs()
+    seed = WORKLOADS[args.workload][2]
+    inputs = make_bases(args.workload, n, seed)
+    if args.workload == "variant":
+        return lambda: O.variant_scores(sd, cfg, inputs[0], inputs[1])
+    X = O.one_hot(inputs[0])
+    return lambda: O.forward(sd, cfg, X)
+
+
+def cpu_forward_rate(args, n_units, min_seconds=10.0, max_reps=8):
+    """Oracle fp32 rate on the host cores, units/s over a bounded sample of
+    n_units units (sequences, or pairs for the variant workload)."""
+    import torch
     cores = len(os.sched_getaffinity(0))
     torch.set_num_threads(cores)
-    torch.manual_seed(0)
-    m = cb.Cherimoya(compile=False)
-    sd = {k: v.clone() for k, v in m.state_dict().items()}
-    cfg = m._init_kwargs()
-    X = make_inputs(n_seqs, 1)
+    run = oracle_step(args, n_units)
     with torch.no_grad():
-        O.forward(sd, cfg, X)                       # warm-up
+        run()                                       # warm-up
         times, t_all = [], time.perf_counter()
         while len(times) < max_reps:
             t0 = time.perf_counter()
-            O.forward(sd, cfg, X)
+            run()
             times.append(time.perf_counter() - t0)
             if time.perf_counter() - t_all >= min_seconds and len(times) >= 2:
                 break
-    return n_seqs / statistics.median(times), cores, len(times)
+    return n_units / statistics.median(times), cores, len(times)
 
 
 def run_reference(args, world, rank):
@@ -179,44 +241,50 @@ def run_reference(args, world, rank):
     if rank != 0:
         return
     import torch
-    from oracle import cherimoya_oracle as O
-    import cherimoya_b200 as cb
     cores = len(os.sched_getaffinity(0))
     torch.set_num_threads(cores)
-    torch.manual_seed(0)
-    m = cb.Cherimoya(compile=False)
-    sd = {k: v.clone() for k, v in m.state_dict().items()}
-    cfg = m._init_kwargs()
     sample = args.ref_sample
-    X = make_inputs(sample, 1)
+    run = oracle_step(args, sample)
+    unit = WORKLOADS[args.workload][3]
     with torch.no_grad():
         for _ in range(args.warmup):
-            O.forward(sd, cfg, X)
+            run()
         t0 = time.perf_counter()
         for _ in range(args.steps):
-            O.forward(sd, cfg, X)
+            run()
         dt = time.perf_counter() - t0
     value = sample * args.steps / dt
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "seqs/s",
+        "impl": "reference", "metric": METRIC, "value": value, "unit": unit,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000.0 * dt / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": workload_config(args, world),
-        "cpu_baseline": {"value": value, "unit": "seqs/s", "cores": cores, "kind": "port",
-                         "sample": "{} of the batch's sequences per step, fp32 eager "
-                                   "no_grad".format(sample)},
-        "e2e": {"value": value, "unit": "seqs/s", "h2d_bytes_per_step": 0,
+        "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": "port",
+                         "sample": "{} of the batch's {} per step, fp32 eager "
+                                   "no_grad".format(sample, unit.split("/")[0])},
+        "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
 def workload_config(args, world):
+    if args.workload == "multitask":
+        what = ("9-layer Cherimoya forward, signal_groups [1, 2, 2, 2, 2] (9 profile tracks, "
+                "5 count heads; random init seed 0), batch {} per GPU of one-hot {}-bp "
+                "sequences with per-sequence GC fraction uniform in [0.35, 0.65], {} mode")
+    elif args.workload == "variant":
+        what = ("ref/alt variant scoring (delta log-count + profile JSD per pair) with the "
+                "12-layer n_filters 256 Cherimoya (trimming 557, random init seed 0), {} "
+                "pairs per GPU of uniform random one-hot {}-bp sequences, alt = one SNV at "
+                "the centre, {} mode")
+    else:
+        what = ("default 9-layer Cherimoya forward (n_filters 128, expansion 2, 1 track, "
+                "random init seed 0), batch {} per GPU of uniform random one-hot {}-bp "
+                "sequences, {} mode")
     return {
-        "workload": "default 9-layer Cherimoya forward (n_filters 128, expansion 2, 1 track, "
-                    "random init seed 0), batch {} per GPU of uniform random one-hot {}-bp "
-                    "sequences, {} mode".format(args.batch, L, args.mode),
+        "workload": what.format(args.batch, L, args.mode),
         "global_batch": args.batch * world, "seq_len": L, "parallelism": "dp{}".format(world),
         "l2": "256 MiB buffer written between timed steps (outside the step events)",
     }
@@ -226,18 +294,30 @@ def run_ours(args, world, rank, local):
     import torch
     import cherimoya_b200 as cb
     from cherimoya_b200 import _lib, ops
+    from oracle.cherimoya_oracle import one_hot  # input generator only
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    torch.manual_seed(0)
-    model = cb.Cherimoya(compile=False, precision=args.mode).eval().to(dev)
-    X = make_inputs(args.batch, 1 + rank).to(dev)
+    model = build_model(args).eval().to(dev)
+    variant = args.workload == "variant"
+    unit = WORKLOADS[args.workload][3]
+    # host inputs: one-hot fp32, (batch, 4, L) each (ref and alt for pairs)
+    host_in = [one_hot(b) for b in make_bases(args.workload, args.batch,
+                                              WORKLOADS[args.workload][2] + rank)]
+    dev_in = [x.to(dev) for x in host_in]
+    forwards = len(host_in)                       # model forwards per unit
+
+    def step(xs):
+        if variant:
+            return cb.variant_effect(model, xs[0], xs[1])
+        return model(xs[0])
+
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
     lib = _lib.load()
 
     with torch.no_grad():
         for _ in range(args.warmup):
-            model(X)
+            step(dev_in)
         torch.cuda.synchronize()
         launches_per_step = ops.last_launch_count()
 
@@ -253,7 +333,7 @@ def run_ours(args, world, rank, local):
         for k in range(args.steps):
             flush.zero_()
             starts[k].record()
-            model(X)
+            step(dev_in)
             ends[k].record()
         torch.cuda.synchronize()
         _lib.timing_enable(False)
@@ -266,25 +346,28 @@ def run_ours(args, world, rank, local):
         value = world * args.batch * args.steps / (dev_ms_max / 1000.0)
 
         # ---- end to end through the public API, host buffers: every step copies
-        # its one-hot input from pinned host memory and reads its outputs back.
-        # The copy of step k+1's input runs on a second stream while step k
-        # computes (two device input buffers), as a serving loop would.
+        # its one-hot inputs from pinned host memory and reads its outputs back.
+        # The copy of step k+1's inputs runs on a second stream while step k
+        # computes (two device buffers per input), as a serving loop would.
         e2e = None
         if not args.no_e2e:
-            Xh = make_inputs(args.batch, 1 + rank).pin_memory()
-            ph = torch.empty((args.batch, 1, L - 2 * model.trimming), dtype=torch.float32,
-                             pin_memory=True)
-            ch = torch.empty((args.batch, 1), dtype=torch.float32, pin_memory=True)
-            xd = [torch.empty_like(Xh, device=dev) for _ in range(2)]
+            hin = [x.pin_memory() for x in host_in]
+            outs = step(dev_in)
+            hout = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in outs]
+            xd = [[torch.empty_like(x, device=dev) for x in hin] for _ in range(2)]
             copy_stream = torch.cuda.Stream(device=dev)
             compute = torch.cuda.current_stream(dev)
+
+            def copy_in(b):
+                for dst, src in zip(xd[b], hin):
+                    dst.copy_(src, non_blocking=True)
 
             def run_steps(n):
                 copied = [torch.cuda.Event() for _ in range(2)]
                 consumed = [torch.cuda.Event() for _ in range(2)]
                 with torch.cuda.stream(copy_stream):
                     copy_stream.wait_stream(compute)       # after the start event
-                    xd[0].copy_(Xh, non_blocking=True)
+                    copy_in(0)
                     copied[0].record(copy_stream)
                 for k in range(n):
                     b = k % 2
@@ -293,13 +376,13 @@ def run_ours(args, world, rank, local):
                         with torch.cuda.stream(copy_stream):
                             if k >= 1:
                                 copy_stream.wait_event(consumed[nb])
-                            xd[nb].copy_(Xh, non_blocking=True)
+                            copy_in(nb)
                             copied[nb].record(copy_stream)
                     compute.wait_event(copied[b])
-                    p, c = model(xd[b])
+                    res = step(xd[b])
                     consumed[b].record(compute)
-                    ph.copy_(p, non_blocking=True)
-                    ch.copy_(c, non_blocking=True)
+                    for h, o in zip(hout, res):
+                        h.copy_(o, non_blocking=True)
 
             run_steps(args.warmup)
             torch.cuda.synchronize()
@@ -312,15 +395,18 @@ def run_ours(args, world, rank, local):
             torch.cuda.synchronize()
             barrier(world)
             e2e_ms = max_over_ranks(e_s.elapsed_time(e_e), world, dev)
+            api = ("cherimoya_b200.variant_effect(model, X_ref, X_alt)" if variant
+                   else "Cherimoya.forward(X)")
             e2e = {"value": world * args.batch * args.steps / (e2e_ms / 1000.0),
-                   "unit": "seqs/s", "h2d_bytes_per_step": Xh.numel() * Xh.element_size(),
-                   "d2h_bytes_per_step": ph.numel() * 4 + ch.numel() * 4,
-                   "api": "Cherimoya.forward(X) on pinned host one-hot fp32 input; the "
-                          "next step's H2D copy overlaps the current step"}
+                   "unit": unit, "h2d_bytes_per_step": sum(x.numel() * x.element_size()
+                                                           for x in hin),
+                   "d2h_bytes_per_step": sum(h.numel() * h.element_size() for h in hout),
+                   "api": api + " on pinned host one-hot fp32 input; the next step's "
+                                "H2D copy overlaps the current step"}
 
         # ---- saturation mutagenesis (sharded by sequence, weak scaling)
         ism = None
-        if args.ism_seqs > 0:
+        if args.ism_seqs > 0 and args.workload == "forward":
             bases = torch.randint(0, 4, (args.ism_seqs, L),
                                   generator=torch.Generator().manual_seed(100 + rank))
             bases = bases.to(torch.int8).to(dev)
@@ -345,35 +431,42 @@ def run_ours(args, world, rank, local):
     peaks, peak_src = load_peaks()
     mlp_ms, mlp_n = per_class["mlp"]
     mlp_avg_ms = mlp_ms / max(mlp_n, 1)
-    mlp_flop = 4.0 * C * H * L * args.batch                 # one layer, one launch
-    achieved = mlp_flop / (mlp_avg_ms / 1000.0) / 1e12
+    # tensor work of the MLP launches of the timed steps over their device time
+    mlp_flop_step = mlp_flop_per_seq(model) * forwards * args.batch
+    achieved = mlp_flop_step * args.steps / (mlp_ms / 1000.0) / 1e12
     peak = peaks["bf16_tflops_sustained"]
-    model_tflops = value / world * FLOP_PER_SEQ / 1e12
+    model_tflops = value / world * forwards * flop_per_seq(model) / 1e12
+    default_width = model.n_filters == 128 and model.expansion == 2
+    C, H = model.n_filters, model.n_filters * model.expansion
     roofline = {
-        "bound": "tensor", "kernel": "mlp_kernel (tcgen05 conv+LN+MLP+residual, one layer)",
+        "bound": "tensor",
+        "kernel": ("mlp_ws_kernel (tcgen05 conv+LN+MLP+residual, one layer)" if default_width
+                   else "mlp_stream_kernel (tcgen05 conv+LN+MLP+residual, one layer)"),
         "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
         "peak_source": "{} bf16_tflops_sustained".format(peak_src),
         "frac_of_burst": achieved / peaks["bf16_tflops"],
-        # DRAM bytes of one MLP launch: ncu dram__bytes_read.sum + write.sum of the
-        # layer-0 launch at batch 256 (138.73 MB + 94.93 MB), scaled by the
-        # sequences processed
-        "traffic": (MLP_DRAM_BYTES_PER_SEQ * args.batch) if args.mode == "bf16" else None,
+        # DRAM bytes of one MLP launch of the default-width backbone: ncu
+        # dram__bytes_read.sum + write.sum of the layer-0 launch at batch 256
+        # (138.73 MB + 94.93 MB), scaled by the sequences processed
+        "traffic": (MLP_DRAM_BYTES_PER_SEQ * args.batch
+                    if args.mode == "bf16" and default_width and not variant else None),
         "traffic_unit": "bytes per launch",
         "algorithmic_bytes": 2.0 * L * C * (2 if args.mode == "bf16" else 4) * args.batch,
-        "flop_per_launch": mlp_flop, "avg_launch_ms": mlp_avg_ms,
+        "flop_per_launch": 4.0 * C * H * L * args.batch, "avg_launch_ms": mlp_avg_ms,
         "whole_forward_tflops_per_gpu": model_tflops,
         "whole_forward_frac": model_tflops / peak,
         "kernel_share": {k: v[0] / max(dev_ms, 1e-9) for k, v in per_class.items() if v[1]},
     }
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        rate, cores, reps = cpu_forward_rate(args.cpu_sample)
-        cpu = {"value": rate, "unit": "seqs/s", "cores": cores, "kind": "port",
-               "sample": "{} sequences, fp32 eager no_grad, median of {} reps".format(
-                   args.cpu_sample, reps)}
+        n_cpu = args.cpu_sample if not variant else max(1, args.cpu_sample // 8)
+        rate, cores, reps = cpu_forward_rate(args, n_cpu)
+        cpu = {"value": rate, "unit": unit, "cores": cores, "kind": "port",
+               "sample": "{} {}, fp32 eager no_grad, median of {} reps".format(
+                   n_cpu, unit.split("/")[0], reps)}
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": "seqs/s", "n_gpus": world,
+            "metric": METRIC, "value": value, "unit": unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": dev_ms_max / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None,
@@ -391,7 +484,9 @@ def main():
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--batch", type=int, default=1024)
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="forward")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="units per GPU per step (default: the workload's)")
     ap.add_argument("--mode", choices=["bf16", "fp32"], default="bf16")
     ap.add_argument("--ism-seqs", type=int, default=4)
     ap.add_argument("--cpu-sample", type=int, default=32)
@@ -399,6 +494,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
+    if args.batch is None:
+        args.batch = WORKLOADS[args.workload][1]
     world, rank, local = dist_setup()
     try:
         if args.impl == "reference":

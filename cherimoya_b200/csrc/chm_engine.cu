@@ -296,6 +296,17 @@ int launch_mlp(const Dims& m, const MlpArgs& a, int grid, cudaStream_t st) {
     }
     return launch_status();
   }
+  if constexpr (sizeof(act_t) == 2) {
+    if (fast && m.CP == wd::kCP && m.HP % 64 == 0 && m.HP <= 512) {
+      // n_filters 256 in bf16: warp-specialised, weights streamed in stages
+      LaunchTimer timer(kKMlp, st);
+      const int wgrid = std::max(1, std::min(a.n_tiles, device_sms()));
+      cudaFuncSetAttribute(mlp_wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(wd::kAlloc));
+      mlp_wide_kernel<<<wgrid, wd::kThreads, wd::kAlloc, st>>>(a);
+      return launch_status();
+    }
+  }
   if (m.CP == 256 || m.HP > 256) {
     // wide models: weights streamed chunk by chunk
     LaunchTimer timer(kKMlp, st);

@@ -1199,6 +1199,337 @@ __global__ void __launch_bounds__(256, 1) mlp_stream_kernel(MlpArgs a) {
   }
 }
 
+// ============================================================== MLP, wide (C = 256), bf16
+// Warp-specialised persistent Cheri Block update for n_filters 256 in bf16
+// mode (any hidden width HP = 64 k <= 512), one CTA per SM, 128-row tiles of
+// the flattened (B * L) rows. W1 and W2 (up to 512 KB) stream from L2 in
+// 32 KB stages, one per MMA group, so the tile's GEMMs are chunked along the
+// hidden dimension (64 units per chunk c):
+//   G1(c): D1[c & 1] = A1 * W1[c]^T     (A1 in shared memory, K = 256, N = 64)
+//   GELU : A2(c) = bf16(gelu(D1[c & 1])) written back into D1's columns
+//   G2(c): D2 (+)= A2(c) * W2[:, c]^T   (A2 from TMEM, K = 64, N = 256)
+// issued as G1(0) G1(1) G2(0) G1(2) G2(1) G1(3) ..., so the GELU of chunk c
+// overlaps G1(c + 1); G1(c + 2) overwrites D1[c & 1] only after G2(c) read it
+// (MMAs of one thread execute in order). Roles (22 warps):
+//   warps 0-7   producer : A1(t + 1) = bf16((conv(X) - mean) * rstd / 2) into
+//                          the other of two shared-memory A1 buffers; lane =
+//                          8 channels of a row (coalesced 512-byte rows)
+//   warps 8-15  GELU     : lane quarter x column half of each D1 chunk
+//   warps 16-19 residual : thread = row; stages the tile's input row as bf16
+//                          in TMEM ahead of time, then X_out = X + bf16(D2)
+//   warp 20     MMA      : one thread issues every tcgen05.mma
+//   warp 21     TMA      : one thread streams the weight stages
+// TMEM: D2 [0,256) | D1[0] [256,320) | D1[1] [320,384) | X stage [384,512).
+// A1 carries the factor 1/2 the GELU of D1/2 expects (gelu_half_bf16x2), as
+// in the default-width kernel. Upstream cheri.py:1072-1082.
+namespace wd {
+constexpr int kCP = 256;
+constexpr int kProducerWarps = 8, kGeluWarps = 8, kResidualWarps = 4;
+constexpr int kGeluWarp0 = kProducerWarps;                      // 8
+constexpr int kResidualWarp0 = kGeluWarp0 + kGeluWarps;         // 16
+constexpr int kMmaWarp = kResidualWarp0 + kResidualWarps;       // 20
+constexpr int kTmaWarp = kMmaWarp + 1;                          // 21
+constexpr int kThreads = (kTmaWarp + 1) * 32;                   // 704
+constexpr uint32_t kA1Bytes = 128 * kCP * 2;                    // 64 KB: 4 K boxes of 16 KB
+constexpr uint32_t kStage = 32768;                              // one weight stage
+constexpr int kStages = 3;
+constexpr uint32_t kA1 = 0;                                     // 2 A1 buffers
+constexpr uint32_t kW = 2 * kA1Bytes;                           // weight ring
+enum Bar : int { A1_FULL0 = 0, A1_FULL1, A1_EMPTY0, A1_EMPTY1, W_FULL0, W_EMPTY0 = W_FULL0 + kStages,
+                 D1_FULL0 = W_EMPTY0 + kStages, D1_FULL1, A2_FULL0, A2_FULL1, D2_FULL, D2_EMPTY,
+                 kNumBars };
+constexpr uint32_t kBars = kW + kStages * kStage;
+constexpr uint32_t kSlot = kBars + kNumBars * 8;
+constexpr uint32_t kAbort = kSlot + 4;
+constexpr uint32_t kAlloc = kAbort + 4 + 1024;
+static_assert(kAlloc <= 232448, "shared memory per block");
+constexpr uint32_t kD2Col = 0, kD1Col = 256, kXsCol = 384;
+}  // namespace wd
+
+__global__ void __launch_bounds__(wd::kThreads, 1) mlp_wide_kernel(MlpArgs a) {
+  using namespace wd;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBars);
+  uint32_t* slot = reinterpret_cast<uint32_t*>(smem + kSlot);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kAbort);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int kChunks = a.HP / 64;
+  const __nv_bfloat16* Xi = static_cast<const __nv_bfloat16*>(a.X_in);
+  __nv_bfloat16* Xo = static_cast<__nv_bfloat16*>(a.X_out);
+
+  if (warp == kMmaWarp) tmem_alloc(slot, 512);
+  if (tid == 0) {
+    for (int i = 0; i < kNumBars; ++i) {
+      uint32_t count = 1;                           // commits, TMA transactions
+      if (i == A1_FULL0 || i == A1_FULL1) count = kProducerWarps;
+      else if (i == A2_FULL0 || i == A2_FULL1) count = kGeluWarps;
+      else if (i == D2_EMPTY) count = kResidualWarps;
+      mbar_init(&bars[i], count);
+    }
+    *abort_flag = 0;
+    mbar_init_fence();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *slot;
+  const int n_my = (a.n_tiles > static_cast<int>(blockIdx.x))
+                       ? (a.n_tiles - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                             static_cast<int>(gridDim.x)
+                       : 0;
+  const int c_total = n_my * kChunks;               // hidden chunks this CTA processes
+  auto row0_of = [&](int it) -> long long {
+    return static_cast<long long>(static_cast<int>(blockIdx.x) + it * static_cast<int>(gridDim.x)) *
+           kTileRows;
+  };
+
+  if (warp < kProducerWarps) {
+    // ------------------------------------------------------------ producer
+    // conv weights of this lane's channels [8 lane, 8 lane + 8) as bf16x2
+    // pairs per tap (zero past C); pairs past C are also masked to 0 in A1
+    const int c0 = 8 * lane;
+    uint32_t w0[4], w1[4], w2[4], cmask[4];
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const int c = c0 + 2 * m;
+      auto wv = [&](int t, int cc) { return cc < a.C ? a.convw[t * kCP + cc] : 0.f; };
+      w0[m] = pack_bf16x2(wv(0, c), wv(0, c + 1));
+      w1[m] = pack_bf16x2(wv(1, c), wv(1, c + 1));
+      w2[m] = pack_bf16x2(wv(2, c), wv(2, c + 1));
+      cmask[m] = (c < a.C ? 0x0000FFFFu : 0u) | (c + 1 < a.C ? 0xFFFF0000u : 0u);
+    }
+    const uint32_t box_off = static_cast<uint32_t>(lane >> 3) * 16384u;   // K box of the lane
+    const int q = lane & 7;                                               // 16-byte chunk in the box row
+    bool ok = true;
+    for (int it = 0; it < n_my && ok; ++it) {
+      const int buf = it & 1;
+      ok = mbar_wait_abortable(&bars[A1_EMPTY0 + buf], ((it >> 1) & 1) ^ 1, abort_flag);
+      if (!ok) break;
+      uint8_t* sA1 = smem + kA1 + buf * kA1Bytes + box_off;
+      const long long row0 = row0_of(it);
+      constexpr int kU = 3;                                  // rows in flight per warp
+      for (int i0 = warp; i0 < kTileRows; i0 += kProducerWarps * kU) {
+        uint4 xl[kU], xc[kU], xr[kU];
+        float2 st[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int rl = i0 + u * kProducerWarps;
+          const long long r = row0 + rl;
+          xl[u] = make_uint4(0u, 0u, 0u, 0u);
+          xc[u] = xl[u];
+          xr[u] = xl[u];
+          st[u] = make_float2(0.f, 0.f);
+          if (rl < kTileRows && r < a.rows) {
+            const int n = static_cast<int>(r / a.L);
+            const int l = static_cast<int>(r - static_cast<long long>(n) * a.L);
+            st[u] = a.stats[n];
+            const uint4* xp = reinterpret_cast<const uint4*>(Xi + r * kCP + c0);
+            xc[u] = __ldg(xp);
+            if (l - a.dil >= 0) xl[u] = __ldg(xp - static_cast<long long>(a.dil) * (kCP / 8));
+            if (l + a.dil < a.L) xr[u] = __ldg(xp + static_cast<long long>(a.dil) * (kCP / 8));
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int rl = i0 + u * kProducerWarps;
+          if (rl >= kTileRows) break;
+          // A1 = (y - mean) * rstd / 2 in bf16x2: y = w0 x[l-d] + w1 x[l] + w2 x[l+d]
+          const uint32_t scale_b = pack_bf16x2(0.5f * st[u].y, 0.5f * st[u].y);
+          const uint32_t shift_b = pack_bf16x2(-0.5f * st[u].x * st[u].y, -0.5f * st[u].x * st[u].y);
+          const uint32_t* pl = &xl[u].x;
+          const uint32_t* pc = &xc[u].x;
+          const uint32_t* pr = &xr[u].x;
+          uint32_t o[4];
+#pragma unroll
+          for (int m = 0; m < 4; ++m) {
+            uint32_t y = bf2_mul(w2[m], pr[m]);
+            y = bf2_fma(w1[m], pc[m], y);
+            y = bf2_fma(w0[m], pl[m], y);
+            o[m] = bf2_fma(y, scale_b, shift_b) & cmask[m];
+          }
+          *reinterpret_cast<uint4*>(sA1 + rl * 128 + ((q ^ (rl & 7)) << 4)) =
+              make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      }
+      fence_async_smem();                          // generic writes -> MMA (async proxy)
+      mbar_arrive_warp(&bars[A1_FULL0 + buf]);
+    }
+  } else if (warp < kResidualWarp0) {
+    // ------------------------------------------------------------ GELU
+    const int quarter = warp & 3, half = (warp - kGeluWarp0) >> 2;
+    const uint32_t lane_sel = static_cast<uint32_t>(quarter * 32) << 16;
+    for (int c = 0; c < c_total; ++c) {
+      const int b = c & 1;
+      if (!mbar_wait_abortable(&bars[D1_FULL0 + b], (c >> 1) & 1, abort_flag)) break;
+      tc_fence_after();
+      // columns [32 half, 32 half + 32) of the chunk, packed in place into
+      // [32 half, 32 half + 16) (already read by this warp)
+      const uint32_t base = tmem + lane_sel + kD1Col + b * 64 + half * 32;
+      uint32_t r[32];
+      tmem_ld32(base, r);
+      uint32_t p[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k)
+        p[k] = gelu_half_bf16x2(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1]));
+      tmem_st16(base, p);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive_warp(&bars[A2_FULL0 + b]);
+    }
+  } else if (warp < kMmaWarp) {
+    // ------------------------------------------------------------ residual
+    const int quarter = warp & 3;
+    const int rl = quarter * 32 + lane;
+    const uint32_t lane_sel = static_cast<uint32_t>(quarter * 32) << 16;
+    for (int it = 0; it < n_my; ++it) {
+      const long long r = row0_of(it) + rl;
+      const bool rv = r < a.rows;
+      // stage this row's input in TMEM (bf16 pairs: 256 channels -> 128
+      // columns), long before D2 is ready
+      const uint4* xp = reinterpret_cast<const uint4*>(Xi + (rv ? r : 0) * kCP);
+#pragma unroll 1
+      for (int g = 0; g < 8; ++g) {                 // 32 channels = 4 x 16 bytes -> 16 columns
+        uint32_t v[16];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint4 a0 = rv ? __ldg(xp + g * 4 + k) : make_uint4(0u, 0u, 0u, 0u);
+          v[4 * k] = a0.x;
+          v[4 * k + 1] = a0.y;
+          v[4 * k + 2] = a0.z;
+          v[4 * k + 3] = a0.w;
+        }
+        tmem_st16(tmem + lane_sel + kXsCol + 16 * g, v);
+      }
+      tmem_st_wait();
+      if (!mbar_wait_abortable(&bars[D2_FULL], it & 1, abort_flag)) break;
+      tc_fence_after();
+      uint4* op = reinterpret_cast<uint4*>(Xo + r * kCP);
+#pragma unroll 1
+      for (int g = 0; g < 8; ++g) {                 // 32 output channels per step
+        uint32_t d[32], x[16];
+        tmem_ld32(tmem + lane_sel + kD2Col + 32 * g, d);
+        tmem_ld16(tmem + lane_sel + kXsCol + 16 * g, x);
+        if (g == 7) {
+          tc_fence_before();
+          mbar_arrive_warp(&bars[D2_EMPTY]);         // D2 fully read
+        }
+        uint32_t o[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k)
+          o[k] = bf2_add(x[k], pack_bf16x2(__uint_as_float(d[2 * k]), __uint_as_float(d[2 * k + 1])));
+        if (rv) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            op[4 * g + k] = make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+        }
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && c_total > 0) {
+      const uint32_t sW = smem_u32(smem + kW);
+      constexpr uint32_t kIdesc1 = idesc_bf16(kTileRows, 64);
+      constexpr uint32_t kIdesc2 = idesc_bf16(kTileRows, kCP);
+      uint32_t k_stage = 0;                          // weight stages consumed
+      bool ok = true;
+      auto stage_in = [&]() -> uint32_t {            // wait for the next weight stage
+        const uint32_t s = k_stage % kStages;
+        ok = ok && mbar_wait_abortable(&bars[W_FULL0 + s], (k_stage / kStages) & 1, abort_flag);
+        return s;
+      };
+      auto g1 = [&](int c) {
+        const int t = c / kChunks, j = c - t * kChunks;
+        if (j == 0) ok = ok && mbar_wait_abortable(&bars[A1_FULL0 + (t & 1)], (t >> 1) & 1, abort_flag);
+        const uint32_t s = stage_in();
+        if (!ok) return;
+        tc_fence_after();
+        const uint32_t sA = smem_u32(smem + kA1 + (t & 1) * kA1Bytes);
+        const uint32_t sB = sW + s * kStage;
+        const uint32_t d = tmem + kD1Col + (c & 1) * 64;
+#pragma unroll
+        for (int k = 0; k < kCP / 16; ++k)
+          mma_bf16(d, desc_sw128(sA + (k >> 2) * 16384 + (k & 3) * 32),
+                   desc_sw128(sB + (k >> 2) * 8192 + (k & 3) * 32), kIdesc1, k > 0 ? 1u : 0u);
+        mma_commit(&bars[W_EMPTY0 + s]);
+        mma_commit(&bars[D1_FULL0 + (c & 1)]);
+        if (j == kChunks - 1) mma_commit(&bars[A1_EMPTY0 + (t & 1)]);
+        ++k_stage;
+      };
+      auto g2 = [&](int c) {
+        const int t = c / kChunks, j = c - t * kChunks;
+        ok = ok && mbar_wait_abortable(&bars[A2_FULL0 + (c & 1)], (c >> 1) & 1, abort_flag);
+        if (j == 0 && t > 0) ok = ok && mbar_wait_abortable(&bars[D2_EMPTY], (t - 1) & 1, abort_flag);
+        const uint32_t s = stage_in();
+        if (!ok) return;
+        tc_fence_after();
+        const uint32_t sB = sW + s * kStage;
+        const uint32_t a2 = tmem + kD1Col + (c & 1) * 64;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)                  // A2 K-step k: half k >> 1, offset 8 (k & 1)
+          mma_bf16_ts(tmem + kD2Col, a2 + 32 * (k >> 1) + 8 * (k & 1),
+                      desc_sw128(sB + k * 32), kIdesc2, (j > 0 || k > 0) ? 1u : 0u);
+        mma_commit(&bars[W_EMPTY0 + s]);
+        if (j == kChunks - 1) mma_commit(&bars[D2_FULL]);
+        ++k_stage;
+      };
+      g1(0);
+      if (c_total > 1) g1(1);
+      for (int c = 0; c < c_total && ok; ++c) {
+        g2(c);
+        if (c + 2 < c_total) g1(c + 2);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ weight TMA
+    // stage order = the MMA issuer's: W1(0) W1(1), then W2(c) W1(c + 2)
+    if (lane == 0 && c_total > 0) {
+      uint32_t k_stage = 0;
+      bool ok = true;
+      auto next = [&]() -> uint8_t* {
+        const uint32_t s = k_stage % kStages;
+        ok = ok && mbar_wait_abortable(&bars[W_EMPTY0 + s], ((k_stage / kStages) & 1) ^ 1, abort_flag);
+        mbar_expect_tx(&bars[W_FULL0 + s], kStage);
+        return smem + kW + s * kStage;
+      };
+      auto load_w1 = [&](int c) {                    // hidden rows [64 j, 64 j + 64), K = 256
+        uint8_t* dst = next();
+        if (!ok) return;
+        const int j = c % kChunks;
+#pragma unroll
+        for (int kb = 0; kb < 4; ++kb)
+          bulk_load(dst + kb * 8192, a.w1 + (static_cast<size_t>(kb) * a.HP + 64 * j) * 128, 8192,
+                    &bars[W_FULL0 + k_stage % kStages]);
+        ++k_stage;
+      };
+      auto load_w2 = [&](int c) {                    // output rows [0, 256), K = hidden chunk j
+        uint8_t* dst = next();
+        if (!ok) return;
+        const int j = c % kChunks;
+        bulk_load(dst, a.w2 + static_cast<size_t>(j) * kCP * 128, kStage,
+                  &bars[W_FULL0 + k_stage % kStages]);
+        ++k_stage;
+      };
+      load_w1(0);
+      if (c_total > 1) load_w1(1);
+      for (int c = 0; c < c_total && ok; ++c) {
+        load_w2(c);
+        if (c + 2 < c_total) load_w1(c + 2);
+      }
+    }
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (tid == 0 && *abort_flag) atomicExch(a.status, kStatusTimeout);
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 // ============================================================== MLP, pipelined
 // Warp-specialised persistent version of mlp_kernel for the default width
 // (C = 128, H = 256). Roles, per CTA (one CTA per SM):
