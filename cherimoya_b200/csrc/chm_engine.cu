@@ -430,23 +430,25 @@ int run_forward_t(const Dims& m, const PackLayout& pl, const uint8_t* packed, in
     const uint8_t* wpk = packed + pl.stem_pk;
     const bool split = (kIn == kInDense) && m.mode == CHM_MODE_FP32;
     LaunchTimer timer(kKStem, st);
-    if (sizeof(act_t) == 2 && m.CP == 128 && !split) {
-      // per-example tiles, TMA-stored output
+    if (sizeof(act_t) == 2 && (m.CP == 128 || m.CP == 256) && !split) {
+      // per-example tiles, TMA-stored output; one launch per 128 output channels
       CUtensorMap tmap;
       CHM_TRY(make_act_tmap3(&tmap, xa, batch, m.L, m.CP));
       const int tiles = batch * ((m.L + kTileRows - 1) / kTileRows);
       const int tgrid =
           std::max(1, std::min((tiles + sm2::kGroups - 1) / sm2::kGroups, device_sms()));
       const int tsmem = static_cast<int>(sm2::smem_bytes(1));
-      auto go = [&](auto k) {
-        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, tsmem);
-        k<<<tgrid, sm2::kThreads, tsmem, st>>>(in, wpk, bias, tmap, batch, m.L, m.C, tiles,
-                                               status);
-      };
-      if (kIn == kInDense) go(stem_tc_kernel<kInDense, 1>);
-      else if (kIn == kInBases) go(stem_tc_kernel<kInBases, 1>);
-      else go(stem_tc_kernel<kInIsm, 1>);
-      CHM_TRY(launch_status());
+      for (int c_off = 0; c_off < m.CP; c_off += 128) {
+        auto go = [&](auto k) {
+          cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, tsmem);
+          k<<<tgrid, sm2::kThreads, tsmem, st>>>(in, wpk, bias, tmap, batch, m.L, m.C, m.CP,
+                                                 c_off, tiles, status);
+        };
+        if (kIn == kInDense) go(stem_tc_kernel<kInDense, 1>);
+        else if (kIn == kInBases) go(stem_tc_kernel<kInBases, 1>);
+        else go(stem_tc_kernel<kInIsm, 1>);
+        CHM_TRY(launch_status());
+      }
     } else {
     const int smem = stem_smem_bytes(m.CP, split ? 2 : 1);
     const int sgrid = std::min(n_tiles, 2 * device_sms());

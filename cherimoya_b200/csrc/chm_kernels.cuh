@@ -425,11 +425,14 @@ __device__ __forceinline__ uint2 bf16x4_hi(const float (&v)[4]) {
   return make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]));
 }
 
+// Output channels [c_off, c_off + 128) of a model with CP padded channels
+// (CP = 128: one launch; CP = 256: two, c_off = 0 and 128). wpk is the packed
+// [hi | lo] weight with CP rows per 128-byte-swizzled K box.
 template <int kIn, int kASplits>
 __global__ void __launch_bounds__(sm2::kThreads, 1) stem_tc_kernel(
     StemInput in, const uint8_t* __restrict__ wpk, const float* __restrict__ bias,
-    const __grid_constant__ CUtensorMap tmap, int batch, int L, int C, int n_tiles,
-    int* status) {
+    const __grid_constant__ CUtensorMap tmap, int batch, int L, int C, int CP, int c_off,
+    int n_tiles, int* status) {
   using namespace sm2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -450,10 +453,18 @@ __global__ void __launch_bounds__(sm2::kThreads, 1) stem_tc_kernel(
     mbar_init_fence();
   }
   {
-    const uint4* src = reinterpret_cast<const uint4*>(wpk);
+    // rows [c_off, c_off + 128) of the hi and lo halves, both K boxes: four
+    // 16 KB pieces [split][box]
     uint4* dst = reinterpret_cast<uint4*>(sB);
-    for (int i = tid; i < static_cast<int>(kW / 16); i += blockDim.x) dst[i] = src[i];
-    if (tid < 128) sbias[tid] = tid < C ? bias[tid] : 0.f;
+    constexpr int kPiece = 128 * 128 / 16;
+    for (int i = tid; i < static_cast<int>(kW / 16); i += blockDim.x) {
+      const int piece = i / kPiece, e = i - piece * kPiece;
+      const int sp = piece >> 1, kb = piece & 1;
+      const size_t off = static_cast<size_t>(sp) * CP * sm::kK * 2 +
+                         static_cast<size_t>(kb) * CP * 128 + static_cast<size_t>(c_off) * 128;
+      dst[i] = reinterpret_cast<const uint4*>(wpk + off)[e];
+    }
+    if (tid < 128) sbias[tid] = c_off + tid < C ? bias[c_off + tid] : 0.f;
   }
   fence_async_smem();
   tc_fence_before();
@@ -554,8 +565,8 @@ __global__ void __launch_bounds__(sm2::kThreads, 1) stem_tc_kernel(
     tc_fence_before();
     named_sync(bar_id, 128);
     if (gt == 0) {
-      tma_store_3d(&tmap, sA, 0, l0, b);
-      tma_store_3d(&tmap, sA + kTileRows * 128, 64, l0, b);
+      tma_store_3d(&tmap, sA, c_off, l0, b);
+      tma_store_3d(&tmap, sA + kTileRows * 128, c_off + 64, l0, b);
       bulk_commit();
     }
   }
