@@ -2540,8 +2540,13 @@ __global__ void __launch_bounds__(hd::kThreads) head_kernel(HeadArgs a) {
 // sum_c X[w, c] lw[g, c] and logcount[g] = lbias[g] + sum_w Z[w, 75 + g] / Lout
 // over the trimmed window. Diagonal sums of the profile are split over two
 // threads per output and combined in a fixed order (deterministic).
+// Warps 0-7 run the epilogue (Z -> ring -> diagonal sums -> profile); warp 8
+// issues the TMA loads and the MMAs, so Z of the next tile is computed while
+// the epilogue works on the current one (two TMEM buffers).
 namespace hd3 {
-constexpr int kThreads = 256;
+constexpr int kEpiThreads = 256;
+constexpr int kIssuerWarp = kEpiThreads / 32;
+constexpr int kThreads = kEpiThreads + 32;
 constexpr int kABufs = 3;
 constexpr int kMaxGroups = hd::kNP - kHeadTaps;          // 5 spare operand rows
 constexpr uint32_t kBox = 128 * 128;                     // 16 KB: 64 channels x 128 rows
@@ -2551,7 +2556,8 @@ constexpr uint32_t kRingOff = kA + kABufs * 2 * kBox;
 constexpr uint32_t kPart = kRingOff + hd::kRing * hd::kZStride * 4;
 constexpr uint32_t kRed = kPart + 2 * 128 * 4;
 constexpr uint32_t kBars = kRed + 8 * kMaxGroups * 4 + 32;
-constexpr uint32_t kSlot = kBars + (kABufs + 2) * 8;
+constexpr int kNumBars = kABufs + 5;                     // a_full[3] z_full[2] z_free[2] mma_done
+constexpr uint32_t kSlot = kBars + kNumBars * 8;
 constexpr uint32_t kAlloc = kSlot + 16 + 1024;
 static_assert(kA % 1024 == 0 && 2 * hd::kNP * 128 * 2 <= kA, "operand layout");
 static_assert(kAlloc <= 232448, "shared memory per block");
@@ -2583,9 +2589,13 @@ __global__ void __launch_bounds__(hd3::kThreads, 1) head_fused_kernel(
                          : 0;
   const int total = n_mine * n_tiles;                   // this CTA's tile sequence
 
+  uint64_t* z_free = z_full + 2;                                        // [2]
+  uint64_t* mma_done = z_free + 2;
   if (warp == 0) tmem_alloc(slot, 256);
   if (tid == 0) {
-    for (int i = 0; i < hd3::kABufs + 2; ++i) mbar_init(&a_full[i], 1);
+    for (int i = 0; i < hd3::kNumBars; ++i) mbar_init(&a_full[i], 1);
+    mbar_init(&z_free[0], hd3::kEpiThreads / 32);
+    mbar_init(&z_free[1], hd3::kEpiThreads / 32);
     mbar_init_fence();
   }
   tc_fence_before();
@@ -2599,145 +2609,169 @@ __global__ void __launch_bounds__(hd3::kThreads, 1) head_fused_kernel(
     o = item / a.batch;
     b = item - o * a.batch;
   };
-  auto load = [&](int g) {
-    int b, o, k;
-    item_of(g, b, o, k);
-    const int buf = g % hd3::kABufs;
-    mbar_expect_tx(&a_full[buf], 2 * kBox);
-    tma_load_3d(sA + buf * 2 * kBox, &tmap, 0, p0 + k * kTileRows, b, &a_full[buf]);
-    tma_load_3d(sA + buf * 2 * kBox + kBox, &tmap, 64, p0 + k * kTileRows, b, &a_full[buf]);
-  };
-  if (tid == 0) {
-    if (total > 0) load(0);
-    if (total > 1) load(1);
-  }
-  const uint32_t sA_addr = smem_u32(sA), sB_addr = smem_u32(sB);
-  const uint32_t idesc = idesc_bf16(kTileRows, kNP);
-  const int rq = warp & 3;                              // TMEM lane quarter
-  const uint32_t lane_sel = static_cast<uint32_t>(rq * 32) << 16;
-  const int w = rq * 32 + lane;                         // tile row of this thread (Z pass)
-  int cur_o = -1;
-  float cnt[hd3::kMaxGroups];
-#pragma unroll
-  for (int gi = 0; gi < hd3::kMaxGroups; ++gi) cnt[gi] = 0.f;
   bool ok = true;
-  for (int g = 0; g < total; ++g) {
-    int b, o, k;
-    item_of(g, b, o, k);
-    if (o != cur_o) {
-      // operand F (hi | lo) of output o; every MMA reading the previous one
-      // has completed (each tile's Z was waited for)
-      const uint4* src = reinterpret_cast<const uint4*>(a.fb + (size_t)o * 2 * kNP * CPH * 2);
-      uint4* dst = reinterpret_cast<uint4*>(sB);
-      for (int i = tid; i < 2 * kNP * CPH * 2 / 16; i += blockDim.x) dst[i] = src[i];
-      fence_async_smem();
-      tc_fence_before();
-      __syncthreads();
-      tc_fence_after();
-      cur_o = o;
+  if (warp == hd3::kIssuerWarp) {
+    // ------------------------------------------------------------ issuer
+    auto load = [&](int g) {
+      int b, o, k;
+      item_of(g, b, o, k);
+      const int buf = g % hd3::kABufs;
+      mbar_expect_tx(&a_full[buf], 2 * kBox);
+      tma_load_3d(sA + buf * 2 * kBox, &tmap, 0, p0 + k * kTileRows, b, &a_full[buf]);
+      tma_load_3d(sA + buf * 2 * kBox + kBox, &tmap, 64, p0 + k * kTileRows, b, &a_full[buf]);
+    };
+    if (lane == 0) {
+      if (total > 0) load(0);
+      if (total > 1) load(1);
     }
-    const int buf = g % hd3::kABufs, zb = g & 1;
-    if (tid == 0) {
-      // A[(g + 2) % 3] was read by the MMA of tile g - 1, complete (waited below)
-      if (g + 2 < total) load(g + 2);
-      ok = mbar_wait(&a_full[buf], (g / hd3::kABufs) & 1);
-      if (ok) {
-        tc_fence_after();
-        uint32_t acc = 0;
-        for (int term = 0; term < 2; ++term) {          // F hi, F lo
+    const uint32_t sA_addr = smem_u32(sA), sB_addr = smem_u32(sB);
+    const uint32_t idesc = idesc_bf16(kTileRows, kNP);
+    int cur_o = -1;
+    uint32_t done_phase = 0;
+    for (int g = 0; g < total && ok; ++g) {
+      int b, o, k;
+      item_of(g, b, o, k);
+      if (o != cur_o) {
+        // operand F (hi | lo) of output o, once the MMAs reading the
+        // previous one have completed
+        if (g > 0) {
+          if (lane == 0) {
+            mma_commit(mma_done);
+            ok = mbar_wait(mma_done, done_phase & 1);
+          }
+          ++done_phase;
+          ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+          if (!ok) break;
+        }
+        const uint4* src = reinterpret_cast<const uint4*>(a.fb + (size_t)o * 2 * kNP * CPH * 2);
+        uint4* dst = reinterpret_cast<uint4*>(sB);
+        for (int i = lane; i < 2 * kNP * CPH * 2 / 16; i += 32) dst[i] = src[i];
+        fence_async_smem();
+        __syncwarp();
+        cur_o = o;
+      }
+      if (lane == 0) {
+        const int buf = g % hd3::kABufs, zb = g & 1;
+        // A[(g + 2) % 3] was last read by the MMA of tile g - 1
+        if (g + 2 < total) {
+          if (g >= 1) ok = mbar_wait(&z_full[(g - 1) & 1], ((g - 1) >> 1) & 1);
+          if (ok) load(g + 2);
+        }
+        ok = ok && mbar_wait(&a_full[buf], (g / hd3::kABufs) & 1);
+        // TMEM buffer zb was released by the epilogue of tile g - 2
+        ok = ok && mbar_wait(&z_free[zb], ((g >> 1) & 1) ^ 1);
+        if (ok) {
+          tc_fence_after();
+          uint32_t acc = 0;
+          for (int term = 0; term < 2; ++term) {          // F hi, F lo
 #pragma unroll
-          for (int kk = 0; kk < CPH / 16; ++kk) {
-            const uint64_t da = desc_sw128(sA_addr + buf * 2 * kBox + (kk >> 2) * kBox +
-                                           (kk & 3) * 32);
-            const uint64_t db = desc_sw128(sB_addr + term * (kNP * CPH * 2) +
-                                           (kk >> 2) * (kNP * 128) + (kk & 3) * 32);
-            mma_bf16(tmem + zb * 128, da, db, idesc, acc);
-            acc = 1;
+            for (int kk = 0; kk < CPH / 16; ++kk) {
+              const uint64_t da = desc_sw128(sA_addr + buf * 2 * kBox + (kk >> 2) * kBox +
+                                             (kk & 3) * 32);
+              const uint64_t db = desc_sw128(sB_addr + term * (kNP * CPH * 2) +
+                                             (kk >> 2) * (kNP * 128) + (kk & 3) * 32);
+              mma_bf16(tmem + zb * 128, da, db, idesc, acc);
+              acc = 1;
+            }
+          }
+          mma_commit(&z_full[zb]);
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int rq = warp & 3;                            // TMEM lane quarter
+    const uint32_t lane_sel = static_cast<uint32_t>(rq * 32) << 16;
+    const int w = rq * 32 + lane;                       // tile row of this thread (Z pass)
+    float cnt[hd3::kMaxGroups];
+#pragma unroll
+    for (int gi = 0; gi < hd3::kMaxGroups; ++gi) cnt[gi] = 0.f;
+    for (int g = 0; g < total; ++g) {
+      int b, o, k;
+      item_of(g, b, o, k);
+      const int zb = g & 1;
+      ok = mbar_wait(&z_full[zb], (g >> 1) & 1);
+      if (!ok) break;
+      tc_fence_after();
+      // ---- Z tile -> ring rows (128 k + w) mod kRing; count columns 75..79
+      {
+        float* zrow = ring + ((k * kTileRows + w) % kRing) * kZStride;
+        uint32_t r[32];
+        if (warp < 4) {
+#pragma unroll 1
+          for (int part_c = 0; part_c < 2; ++part_c) {
+            tmem_ld32(tmem + zb * 128 + lane_sel + part_c * 32, r);
+#pragma unroll
+            for (int q = 0; q < 32; ++q) zrow[part_c * 32 + q] = __uint_as_float(r[q]);
+          }
+        } else {
+          tmem_ld32(tmem + zb * 128 + lane_sel + 48, r);   // columns 48..79
+#pragma unroll
+          for (int q = 16; q < 32; ++q) {
+            const int t = 48 + q;
+            if (t < kHeadTaps) zrow[t] = __uint_as_float(r[q]);
+          }
+          const int wr = k * kTileRows + w;                // window row
+          if (o == 0 && wr >= kHeadPad && wr < kHeadPad + a.Lout) {
+#pragma unroll
+            for (int gi = 0; gi < hd3::kMaxGroups; ++gi)
+              cnt[gi] += __uint_as_float(r[kHeadTaps - 48 + gi]);
           }
         }
-        mma_commit(&z_full[zb]);
       }
-    }
-    if (__syncthreads_or(!ok)) break;
-    ok = mbar_wait(&z_full[zb], (g >> 1) & 1);
-    if (__syncthreads_or(!ok)) break;
-    tc_fence_after();
-    // ---- Z tile -> ring rows (128 k + w) mod kRing; count columns 75..79
-    {
-      float* zrow = ring + ((k * kTileRows + w) % kRing) * kZStride;
-      uint32_t r[32];
-      if (warp < 4) {
-#pragma unroll 1
-        for (int part_c = 0; part_c < 2; ++part_c) {
-          tmem_ld32(tmem + zb * 128 + lane_sel + part_c * 32, r);
-#pragma unroll
-          for (int q = 0; q < 32; ++q) zrow[part_c * 32 + q] = __uint_as_float(r[q]);
-        }
-      } else {
-        tmem_ld32(tmem + zb * 128 + lane_sel + 48, r);   // columns 48..79
-#pragma unroll
-        for (int q = 16; q < 32; ++q) {
-          const int t = 48 + q;
-          if (t < kHeadTaps) zrow[t] = __uint_as_float(r[q]);
-        }
-        const int wr = k * kTileRows + w;                // window row
-        if (o == 0 && wr >= kHeadPad && wr < kHeadPad + a.Lout) {
-#pragma unroll
-          for (int gi = 0; gi < hd3::kMaxGroups; ++gi)
-            cnt[gi] += __uint_as_float(r[kHeadTaps - 48 + gi]);
-        }
-      }
-    }
-    tc_fence_before();
-    __syncthreads();
-    // ---- diagonal sums: output j = sum_t ring[(j + t) mod kRing][t], two halves
-    const int j_lo = (k == 0) ? 0 : k * kTileRows - (kHeadTaps - 1);
-    const int j_hi = (k == n_tiles - 1) ? a.Lout
-                                        : min(a.Lout, k * kTileRows + kTileRows - (kHeadTaps - 1));
-    {
-      const int jj = tid & 127, half = tid >> 7;
-      const int j = j_lo + jj;
-      if (j < j_hi) {
-        const int t0 = half ? 38 : 0, t1 = half ? kHeadTaps : 38;
-        int rrow = (j + t0) % kRing;
-        float acc = 0.f;
+      tc_fence_before();
+      mbar_arrive_warp(&z_free[zb]);                      // TMEM buffer zb is free again
+      named_sync(1, hd3::kEpiThreads);
+      // ---- diagonal sums: output j = sum_t ring[(j + t) mod kRing][t], two halves
+      const int j_lo = (k == 0) ? 0 : k * kTileRows - (kHeadTaps - 1);
+      const int j_hi = (k == n_tiles - 1) ? a.Lout
+                                          : min(a.Lout, k * kTileRows + kTileRows - (kHeadTaps - 1));
+      {
+        const int jj = tid & 127, half = tid >> 7;
+        const int j = j_lo + jj;
+        if (j < j_hi) {
+          const int t0 = half ? 38 : 0, t1 = half ? kHeadTaps : 38;
+          int rrow = (j + t0) % kRing;
+          float acc = 0.f;
 #pragma unroll 4
-        for (int t = t0; t < t1; ++t) {
-          acc += ring[rrow * kZStride + t];
-          rrow = (rrow + 1 == kRing) ? 0 : rrow + 1;
-        }
-        part[half * 128 + jj] = acc;
-      }
-    }
-    __syncthreads();
-    if (tid < 128) {
-      const int j = j_lo + tid;
-      if (j < j_hi)
-        a.profile[((long long)b * a.n_out + o) * a.Lout + j] =
-            (part[tid] + part[128 + tid]) + a.fbias[o];
-    }
-    // ---- count head at the end of an item of output 0: fixed-order reduction
-    if (o == 0 && k == n_tiles - 1) {
-      if (warp >= 4) {
-#pragma unroll
-        for (int gi = 0; gi < hd3::kMaxGroups; ++gi) {
-          float v = cnt[gi];
-#pragma unroll
-          for (int sh = 16; sh > 0; sh >>= 1) v += __shfl_xor_sync(0xffffffffu, v, sh);
-          if (lane == 0) red[(warp - 4) * hd3::kMaxGroups + gi] = v;
-          cnt[gi] = 0.f;
+          for (int t = t0; t < t1; ++t) {
+            acc += ring[rrow * kZStride + t];
+            rrow = (rrow + 1 == kRing) ? 0 : rrow + 1;
+          }
+          part[half * 128 + jj] = acc;
         }
       }
-      __syncthreads();
-      if (tid < a.n_groups) {
-        const float s4 = ((red[tid] + red[hd3::kMaxGroups + tid]) +
-                          red[2 * hd3::kMaxGroups + tid]) + red[3 * hd3::kMaxGroups + tid];
-        a.logcounts[(long long)b * a.n_groups + tid] =
-            a.lbias[tid] + s4 / static_cast<float>(a.Lout);
+      named_sync(1, hd3::kEpiThreads);
+      if (tid < 128) {
+        const int j = j_lo + tid;
+        if (j < j_hi)
+          a.profile[((long long)b * a.n_out + o) * a.Lout + j] =
+              (part[tid] + part[128 + tid]) + a.fbias[o];
+      }
+      // ---- count head at the end of an item of output 0: fixed-order reduction
+      if (o == 0 && k == n_tiles - 1) {
+        if (warp >= 4) {
+#pragma unroll
+          for (int gi = 0; gi < hd3::kMaxGroups; ++gi) {
+            float v = cnt[gi];
+#pragma unroll
+            for (int sh = 16; sh > 0; sh >>= 1) v += __shfl_xor_sync(0xffffffffu, v, sh);
+            if (lane == 0) red[(warp - 4) * hd3::kMaxGroups + gi] = v;
+            cnt[gi] = 0.f;
+          }
+        }
+        named_sync(1, hd3::kEpiThreads);
+        if (tid < a.n_groups) {
+          const float s4 = ((red[tid] + red[hd3::kMaxGroups + tid]) +
+                            red[2 * hd3::kMaxGroups + tid]) + red[3 * hd3::kMaxGroups + tid];
+          a.logcounts[(long long)b * a.n_groups + tid] =
+              a.lbias[tid] + s4 / static_cast<float>(a.Lout);
+        }
       }
     }
   }
-  if (!ok && tid == 0) atomicExch(a.status, kStatusTimeout);
+  if (!ok) atomicExch(a.status, kStatusTimeout);
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
