@@ -511,15 +511,18 @@ int run_forward_t(const Dims& m, const PackLayout& pl, const uint8_t* packed, in
   h.L = m.L; h.C = m.C; h.CP = m.CP; h.CPH = cph; h.n_ctl = m.n_ctl; h.n_out = m.n_out;
   h.n_groups = m.n_groups; h.T = m.T; h.Lout = m.Lout;
   h.batch = batch;
-  if (sizeof(act_t) == 2 && m.n_ctl == 0 && m.CP == 128 && cph == 128 &&
+  if (sizeof(act_t) == 2 && m.n_ctl == 0 && (m.CP == 128 || m.CP == 256) && cph == m.CP &&
       m.n_groups <= hd3::kMaxGroups) {
     CUtensorMap tmap;
     CHM_TRY(make_act_tmap3(&tmap, xa, batch, m.L, m.CP));
-    cudaFuncSetAttribute(head_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         hd3::kAlloc);
     const int hgrid = std::max(1, std::min(batch * m.n_out, device_sms()));
     LaunchTimer timer(kKProfile, st);
-    head_fused_kernel<<<hgrid, hd3::kThreads, hd3::kAlloc, st>>>(h, tmap);
+    auto go = [&](auto k) {
+      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, hd3::kAlloc);
+      k<<<hgrid, hd3::kThreads, hd3::kAlloc, st>>>(h, tmap);
+    };
+    if (m.CP == 128) go(head_fused_kernel<128>);
+    else go(head_fused_kernel<256>);
     CHM_TRY(launch_status());
   } else if (!(cph == 256 && split_a)) {
     const int smem = head_smem_bytes(cph, split_a ? 2 : 1);

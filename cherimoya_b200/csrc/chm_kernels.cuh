@@ -2309,6 +2309,22 @@ constexpr int kNP = 80;            // 75 taps padded to an MMA N
 constexpr int kZStride = 77;       // Z ring row stride (floats): conflict-free diagonals
 constexpr int kRing = 208;         // ring rows: one tile + the 74-row halo, rounded up
 constexpr int kThreads = 128;
+
+// sum over u < n of ring[((row0 + u) mod kRing) * kZStride + t0 + u], in order
+// of u (row0 < kRing): consecutive taps of one output are one ring row and one
+// column apart, a stride of kZStride + 1 floats, with at most one wrap of the
+// ring in between
+__device__ __forceinline__ float ring_diag_sum(const float* ring, int row0, int t0, int n) {
+  const int n1 = min(n, kRing - row0);
+  const float* p = ring + row0 * kZStride + t0;
+  float acc = 0.f;
+#pragma unroll 4
+  for (int u = 0; u < n1; ++u) acc += p[u * (kZStride + 1)];
+  const float* q = ring + t0 + n1;
+#pragma unroll 4
+  for (int u = 0; u < n - n1; ++u) acc += q[u * (kZStride + 1)];
+  return acc;
+}
 }  // namespace hd
 
 struct HeadArgs {
@@ -2476,13 +2492,7 @@ __global__ void __launch_bounds__(hd::kThreads) head_kernel(HeadArgs a) {
     const int j_hi = (k == n_tiles - 1) ? a.Lout
                                         : min(a.Lout, k * kTileRows + kTileRows - (kHeadTaps - 1));
     for (int j = j_lo + tid; j < j_hi; j += blockDim.x) {
-      float acc = 0.f;
-      int rrow = j % kRing;
-#pragma unroll 5
-      for (int t = 0; t < kHeadTaps; ++t) {
-        acc += ring[rrow * kZStride + t];
-        rrow = (rrow + 1 == kRing) ? 0 : rrow + 1;
-      }
+      const float acc = ring_diag_sum(ring, j % kRing, 0, kHeadTaps);
       a.profile[((long long)b * a.n_out + o) * a.Lout + j] = acc + a.fbias[o];
     }
     __syncthreads();
@@ -2556,21 +2566,29 @@ constexpr uint32_t kRingOff = kA + kABufs * 2 * kBox;
 constexpr uint32_t kPart = kRingOff + hd::kRing * hd::kZStride * 4;
 constexpr uint32_t kRed = kPart + 2 * 128 * 4;
 constexpr uint32_t kBars = kRed + 8 * kMaxGroups * 4 + 32;
-constexpr int kNumBars = kABufs + 5;                     // a_full[3] z_full[2] z_free[2] mma_done
+constexpr int kNumBars = 2 * kABufs + 5;  // a_full[3] z_full[2] z_free[2] mma_done a_free[3]
 constexpr uint32_t kSlot = kBars + kNumBars * 8;
 constexpr uint32_t kAlloc = kSlot + 16 + 1024;
 static_assert(kA % 1024 == 0 && 2 * hd::kNP * 128 * 2 <= kA, "operand layout");
 static_assert(kAlloc <= 232448, "shared memory per block");
 }  // namespace hd3
 
+// CPH = 128: F as bf16 hi + lo (two MMA terms); CPH = 256: each window tile
+// arrives in two 128-channel halves that accumulate into the same Z, and F is
+// bf16 (the precision of the upstream bf16 autocast path for this conv), so
+// the shared-memory layout is the same for both widths.
+template <int CPH>
 __global__ void __launch_bounds__(hd3::kThreads, 1) head_fused_kernel(
     HeadArgs a, const __grid_constant__ CUtensorMap tmap) {
   using namespace hd;
   using hd3::kBox;
+  static_assert(CPH == 128 || CPH == 256, "head width");
+  constexpr int kSub = CPH / 128;                       // 128-channel halves per tile
+  constexpr int kTerms = CPH == 128 ? 2 : 1;            // F hi (+ lo)
+  static_assert(kTerms * kNP * CPH * 2 <= hd3::kA, "operand F");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  constexpr int CPH = 128;
   uint8_t* sB = smem + hd3::kB;
   uint8_t* sA = smem + hd3::kA;
   float* ring = reinterpret_cast<float*>(smem + hd3::kRingOff);
@@ -2591,6 +2609,7 @@ __global__ void __launch_bounds__(hd3::kThreads, 1) head_fused_kernel(
 
   uint64_t* z_free = z_full + 2;                                        // [2]
   uint64_t* mma_done = z_free + 2;
+  uint64_t* a_free = mma_done + 1;                                      // [kABufs]
   if (warp == 0) tmem_alloc(slot, 256);
   if (tid == 0) {
     for (int i = 0; i < hd3::kNumBars; ++i) mbar_init(&a_full[i], 1);
@@ -2612,17 +2631,20 @@ __global__ void __launch_bounds__(hd3::kThreads, 1) head_fused_kernel(
   bool ok = true;
   if (warp == hd3::kIssuerWarp) {
     // ------------------------------------------------------------ issuer
-    auto load = [&](int g) {
+    // sub-step gs = (tile g, channel half gs % kSub) -> A buffer gs % kABufs
+    const int total_sub = total * kSub;
+    auto load = [&](int gs) {
       int b, o, k;
-      item_of(g, b, o, k);
-      const int buf = g % hd3::kABufs;
+      item_of(gs / kSub, b, o, k);
+      const int buf = gs % hd3::kABufs, x0 = 128 * (gs % kSub);
       mbar_expect_tx(&a_full[buf], 2 * kBox);
-      tma_load_3d(sA + buf * 2 * kBox, &tmap, 0, p0 + k * kTileRows, b, &a_full[buf]);
-      tma_load_3d(sA + buf * 2 * kBox + kBox, &tmap, 64, p0 + k * kTileRows, b, &a_full[buf]);
+      tma_load_3d(sA + buf * 2 * kBox, &tmap, x0, p0 + k * kTileRows, b, &a_full[buf]);
+      tma_load_3d(sA + buf * 2 * kBox + kBox, &tmap, x0 + 64, p0 + k * kTileRows, b,
+                  &a_full[buf]);
     };
     if (lane == 0) {
-      if (total > 0) load(0);
-      if (total > 1) load(1);
+      if (total_sub > 0) load(0);
+      if (total_sub > 1) load(1);
     }
     const uint32_t sA_addr = smem_u32(sA), sB_addr = smem_u32(sB);
     const uint32_t idesc = idesc_bf16(kTileRows, kNP);
@@ -2632,8 +2654,8 @@ __global__ void __launch_bounds__(hd3::kThreads, 1) head_fused_kernel(
       int b, o, k;
       item_of(g, b, o, k);
       if (o != cur_o) {
-        // operand F (hi | lo) of output o, once the MMAs reading the
-        // previous one have completed
+        // operand F of output o, once the MMAs reading the previous one have
+        // completed
         if (g > 0) {
           if (lane == 0) {
             mma_commit(mma_done);
@@ -2645,36 +2667,39 @@ __global__ void __launch_bounds__(hd3::kThreads, 1) head_fused_kernel(
         }
         const uint4* src = reinterpret_cast<const uint4*>(a.fb + (size_t)o * 2 * kNP * CPH * 2);
         uint4* dst = reinterpret_cast<uint4*>(sB);
-        for (int i = lane; i < 2 * kNP * CPH * 2 / 16; i += 32) dst[i] = src[i];
+        for (int i = lane; i < kTerms * kNP * CPH * 2 / 16; i += 32) dst[i] = src[i];
         fence_async_smem();
         __syncwarp();
         cur_o = o;
       }
       if (lane == 0) {
-        const int buf = g % hd3::kABufs, zb = g & 1;
-        // A[(g + 2) % 3] was last read by the MMA of tile g - 1
-        if (g + 2 < total) {
-          if (g >= 1) ok = mbar_wait(&z_full[(g - 1) & 1], ((g - 1) >> 1) & 1);
-          if (ok) load(g + 2);
-        }
-        ok = ok && mbar_wait(&a_full[buf], (g / hd3::kABufs) & 1);
-        // TMEM buffer zb was released by the epilogue of tile g - 2
-        ok = ok && mbar_wait(&z_free[zb], ((g >> 1) & 1) ^ 1);
-        if (ok) {
+        const int zb = g & 1;
+        for (int half = 0; half < kSub && ok; ++half) {
+          const int gs = g * kSub + half, buf = gs % hd3::kABufs;
+          // A[(gs + 2) % 3] was last read by the MMAs of sub-step gs - 1
+          if (gs + 2 < total_sub) {
+            if (gs >= 1)
+              ok = mbar_wait(&a_free[(gs - 1) % hd3::kABufs], ((gs - 1) / hd3::kABufs) & 1);
+            if (ok) load(gs + 2);
+          }
+          ok = ok && mbar_wait(&a_full[buf], (gs / hd3::kABufs) & 1);
+          // TMEM buffer zb was released by the epilogue of tile g - 2
+          if (half == 0) ok = ok && mbar_wait(&z_free[zb], ((g >> 1) & 1) ^ 1);
+          if (!ok) break;
           tc_fence_after();
-          uint32_t acc = 0;
-          for (int term = 0; term < 2; ++term) {          // F hi, F lo
+          for (int term = 0; term < kTerms; ++term) {    // F hi (, F lo)
 #pragma unroll
-            for (int kk = 0; kk < CPH / 16; ++kk) {
+            for (int kk = 0; kk < 8; ++kk) {
               const uint64_t da = desc_sw128(sA_addr + buf * 2 * kBox + (kk >> 2) * kBox +
                                              (kk & 3) * 32);
               const uint64_t db = desc_sw128(sB_addr + term * (kNP * CPH * 2) +
-                                             (kk >> 2) * (kNP * 128) + (kk & 3) * 32);
-              mma_bf16(tmem + zb * 128, da, db, idesc, acc);
-              acc = 1;
+                                             (2 * half + (kk >> 2)) * (kNP * 128) + (kk & 3) * 32);
+              mma_bf16(tmem + zb * 128, da, db, idesc,
+                       (half > 0 || term > 0 || kk > 0) ? 1u : 0u);
             }
           }
-          mma_commit(&z_full[zb]);
+          mma_commit(&a_free[buf]);
+          if (half == kSub - 1) mma_commit(&z_full[zb]);
         }
       }
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
@@ -2732,14 +2757,7 @@ __global__ void __launch_bounds__(hd3::kThreads, 1) head_fused_kernel(
         const int j = j_lo + jj;
         if (j < j_hi) {
           const int t0 = half ? 38 : 0, t1 = half ? kHeadTaps : 38;
-          int rrow = (j + t0) % kRing;
-          float acc = 0.f;
-#pragma unroll 4
-          for (int t = t0; t < t1; ++t) {
-            acc += ring[rrow * kZStride + t];
-            rrow = (rrow + 1 == kRing) ? 0 : rrow + 1;
-          }
-          part[half * 128 + jj] = acc;
+          part[half * 128 + jj] = ring_diag_sum(ring, (j + t0) % kRing, t0, t1 - t0);
         }
       }
       named_sync(1, hd3::kEpiThreads);
