@@ -440,8 +440,9 @@ def run_ours(args, world, rank, local):
     C, H = model.n_filters, model.n_filters * model.expansion
     roofline = {
         "bound": "tensor",
-        "kernel": ("mlp_ws_kernel (tcgen05 conv+LN+MLP+residual, one layer)" if default_width
-                   else "mlp_stream_kernel (tcgen05 conv+LN+MLP+residual, one layer)"),
+        "kernel": ("mlp_ws_kernel" if default_width
+                   else "mlp_wide_kernel" if C == 256 and args.mode == "bf16"
+                   else "mlp_stream_kernel") + " (tcgen05 conv+LN+MLP+residual, one layer)",
         "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
         "peak_source": "{} bf16_tflops_sustained".format(peak_src),
         "frac_of_burst": achieved / peaks["bf16_tflops"],
