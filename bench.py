@@ -363,6 +363,8 @@ def run_ours(args, world, rank, local):
                     dst.copy_(src, non_blocking=True)
 
             def run_steps(n):
+                # copy stream: input H2D of the next step and output D2H of the
+                # finished one, both overlapping the compute of the current step
                 copied = [torch.cuda.Event() for _ in range(2)]
                 consumed = [torch.cuda.Event() for _ in range(2)]
                 with torch.cuda.stream(copy_stream):
@@ -381,8 +383,12 @@ def run_ours(args, world, rank, local):
                     compute.wait_event(copied[b])
                     res = step(xd[b])
                     consumed[b].record(compute)
-                    for h, o in zip(hout, res):
-                        h.copy_(o, non_blocking=True)
+                    with torch.cuda.stream(copy_stream):
+                        copy_stream.wait_event(consumed[b])
+                        for h, o in zip(hout, res):
+                            o.record_stream(copy_stream)
+                            h.copy_(o, non_blocking=True)
+                compute.wait_stream(copy_stream)           # before the end event
 
             run_steps(args.warmup)
             torch.cuda.synchronize()

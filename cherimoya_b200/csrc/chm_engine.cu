@@ -343,6 +343,27 @@ int launch_mlp(const Dims& m, const MlpArgs& a, int grid, cudaStream_t st) {
   return CHM_ERR_UNSUPPORTED;
 }
 
+// Per-example statistics with each thread reading the three conv rows of its
+// positions directly (any activation type).
+template <typename act_t>
+int launch_stats_direct(const Dims& m, const act_t* X, const float* convw, int dil, int batch,
+                        float2* stats, cudaStream_t st) {
+  LaunchTimer timer(kKStats, st);
+  if (m.CP == 64) {
+    stats_example_kernel<act_t, 64><<<batch, kStats2Threads, 0, st>>>(X, convw, dil, m.L, m.C,
+                                                                      1e-3f, stats);
+  } else if (m.CP == 128) {
+    stats_example_kernel<act_t, 128><<<batch, kStats2Threads, 0, st>>>(X, convw, dil, m.L, m.C,
+                                                                       1e-3f, stats);
+  } else if (m.CP == 256) {
+    stats_example_kernel<act_t, 256><<<batch, kStats2Threads, 0, st>>>(X, convw, dil, m.L, m.C,
+                                                                       1e-3f, stats);
+  } else {
+    return CHM_ERR_UNSUPPORTED;
+  }
+  return launch_status();
+}
+
 template <typename act_t>
 int launch_stats(const Dims& m, const act_t* X, const float* convw, int dil, int batch,
                  float* partials, unsigned* counters, float2* stats, int* status,
@@ -354,6 +375,9 @@ int launch_stats(const Dims& m, const act_t* X, const float* convw, int dil, int
     // avoid dead slots when the chains are short (large dilation); pick the
     // length with the fewest load slots plus per-segment overhead
     const int K = (m.L + dil - 1) / dil;            // longest chain
+    // chains of at most 4 rows (d >= L / 4): the halo rows outnumber the
+    // chain rows, so read the three rows of each position directly
+    if (K <= 4) return launch_stats_direct<act_t>(m, X, convw, dil, batch, stats, st);
     static const int kLens[] = {4, 6, 8, 9, 12};
     int kS = 4;
     long best = -1;
@@ -392,20 +416,7 @@ int launch_stats(const Dims& m, const act_t* X, const float* convw, int dil, int
     }
     return launch_status();
   }
-  LaunchTimer timer(kKStats, st);
-  if (m.CP == 64) {
-    stats_example_kernel<act_t, 64><<<batch, kStats2Threads, 0, st>>>(X, convw, dil, m.L, m.C,
-                                                                      1e-3f, stats);
-  } else if (m.CP == 128) {
-    stats_example_kernel<act_t, 128><<<batch, kStats2Threads, 0, st>>>(X, convw, dil, m.L, m.C,
-                                                                       1e-3f, stats);
-  } else if (m.CP == 256) {
-    stats_example_kernel<act_t, 256><<<batch, kStats2Threads, 0, st>>>(X, convw, dil, m.L, m.C,
-                                                                       1e-3f, stats);
-  } else {
-    return CHM_ERR_UNSUPPORTED;
-  }
-  return launch_status();
+  return launch_stats_direct<act_t>(m, X, convw, dil, batch, stats, st);
 }
 
 // The whole forward for `batch` rows whose stem input is `in` (kind kIn).
