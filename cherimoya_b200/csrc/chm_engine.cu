@@ -74,7 +74,6 @@ struct Dims {
   int C, CP, H, HP, L, T, Lout, n_layers, n_out, n_groups, n_ctl, mode;
   float rs;
   int act_bytes() const { return mode == CHM_MODE_BF16 ? 2 : 4; }
-  int n_chunks() const { return (L + kStatsRows - 1) / kStatsRows; }
 };
 
 Dims dims_of(const chm_model_desc* d) {
@@ -130,16 +129,14 @@ PackLayout pack_layout(const Dims& m) {
 
 // ---- forward workspace layout (for `batch` rows)
 struct FwdLayout {
-  size_t status, counters, stats, partials, xa, xb, total;
+  size_t status, stats, xa, xb, total;
 };
 
 FwdLayout fwd_layout(const Dims& m, int batch) {
   FwdLayout f;
   size_t o = 0;
   f.status = o; o = align_up(o + 256);
-  f.counters = o; o = align_up(o + (size_t)batch * 4);
   f.stats = o; o = align_up(o + (size_t)batch * 8);
-  f.partials = o; o = align_up(o + (size_t)batch * m.n_chunks() * 12);
   const size_t act = (size_t)batch * m.L * m.CP * m.act_bytes();
   f.xa = o; o = align_up(o + act);
   f.xb = o; o = align_up(o + act);
@@ -153,6 +150,33 @@ int device_sms() {
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
   return sms > 0 ? sms : 148;
 }
+
+// Launch `k`; with `pdl` under programmatic stream serialization, so the grid
+// may start while the stream's previous kernel finishes. Such a kernel calls
+// griddep_wait() before it touches anything an earlier kernel of the stream
+// wrote; before that it reads only packed weights. The first kernel of every
+// C-ABI call is launched without it, so weight packing that precedes a call
+// has completed before any of the call's kernels reads the weights.
+template <typename... KArgs, typename... Args>
+void launch_k(bool pdl, void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem,
+              cudaStream_t st, Args... args) {
+  if (!pdl) {
+    k<<<grid, block, smem, st>>>(args...);
+    return;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, k, args...);
+}
+
 
 int launch_status() {
   ++g_launches;
@@ -274,7 +298,7 @@ int launch_mlp(const Dims& m, const MlpArgs& a, int grid, cudaStream_t st) {
     LaunchTimer timer(kKMlp, st);
     auto go = [&](auto k, int smem) {
       cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      k<<<egrid, ws::kThreads, smem, st>>>(ae, tmap);
+      launch_k(true, k, dim3(egrid), dim3(ws::kThreads), smem, st, ae, tmap);
     };
     bool wide = false;
     if constexpr (sizeof(act_t) == 2) {
@@ -303,7 +327,7 @@ int launch_mlp(const Dims& m, const MlpArgs& a, int grid, cudaStream_t st) {
       const int wgrid = std::max(1, std::min(a.n_tiles, device_sms()));
       cudaFuncSetAttribute(mlp_wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(wd::kAlloc));
-      mlp_wide_kernel<<<wgrid, wd::kThreads, wd::kAlloc, st>>>(a);
+      launch_k(true, mlp_wide_kernel, dim3(wgrid), dim3(wd::kThreads), wd::kAlloc, st, a);
       return launch_status();
     }
   }
@@ -347,17 +371,17 @@ int launch_mlp(const Dims& m, const MlpArgs& a, int grid, cudaStream_t st) {
 // positions directly (any activation type).
 template <typename act_t>
 int launch_stats_direct(const Dims& m, const act_t* X, const float* convw, int dil, int batch,
-                        float2* stats, cudaStream_t st) {
+                        float2* stats, bool pdl, cudaStream_t st) {
   LaunchTimer timer(kKStats, st);
   if (m.CP == 64) {
-    stats_example_kernel<act_t, 64><<<batch, kStats2Threads, 0, st>>>(X, convw, dil, m.L, m.C,
-                                                                      1e-3f, stats);
+    launch_k(pdl, stats_example_kernel<act_t, 64>, dim3(batch), dim3(kStats2Threads), 0, st, X,
+             convw, dil, m.L, m.C, 1e-3f, stats);
   } else if (m.CP == 128) {
-    stats_example_kernel<act_t, 128><<<batch, kStats2Threads, 0, st>>>(X, convw, dil, m.L, m.C,
-                                                                       1e-3f, stats);
+    launch_k(pdl, stats_example_kernel<act_t, 128>, dim3(batch), dim3(kStats2Threads), 0, st, X,
+             convw, dil, m.L, m.C, 1e-3f, stats);
   } else if (m.CP == 256) {
-    stats_example_kernel<act_t, 256><<<batch, kStats2Threads, 0, st>>>(X, convw, dil, m.L, m.C,
-                                                                       1e-3f, stats);
+    launch_k(pdl, stats_example_kernel<act_t, 256>, dim3(batch), dim3(kStats2Threads), 0, st, X,
+             convw, dil, m.L, m.C, 1e-3f, stats);
   } else {
     return CHM_ERR_UNSUPPORTED;
   }
@@ -366,10 +390,7 @@ int launch_stats_direct(const Dims& m, const act_t* X, const float* convw, int d
 
 template <typename act_t>
 int launch_stats(const Dims& m, const act_t* X, const float* convw, int dil, int batch,
-                 float* partials, unsigned* counters, float2* stats, int* status,
-                 cudaStream_t st) {
-  (void)partials;
-  (void)counters;
+                 float2* stats, bool pdl, cudaStream_t st) {
   if constexpr (sizeof(act_t) == 2) {
     // segment length: long segments amortise the two halo rows, short ones
     // avoid dead slots when the chains are short (large dilation); pick the
@@ -377,7 +398,7 @@ int launch_stats(const Dims& m, const act_t* X, const float* convw, int dil, int
     const int K = (m.L + dil - 1) / dil;            // longest chain
     // chains of at most 4 rows (d >= L / 4): the halo rows outnumber the
     // chain rows, so read the three rows of each position directly
-    if (K <= 4) return launch_stats_direct<act_t>(m, X, convw, dil, batch, stats, st);
+    if (K <= 4) return launch_stats_direct<act_t>(m, X, convw, dil, batch, stats, pdl, st);
     static const int kLens[] = {4, 6, 8, 9, 12};
     int kS = 4;
     long best = -1;
@@ -392,8 +413,9 @@ int launch_stats(const Dims& m, const act_t* X, const float* convw, int dil, int
     const int n_kb = (K + kS - 1) / kS;
     LaunchTimer timer(kKStats, st);
     auto go = [&](auto kern) {
-      kern<<<batch, kStatsChainThreads, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(X), convw,
-                                                 dil, m.L, m.C, n_kb, 1e-3f, stats);
+      launch_k(pdl, kern, dim3(batch), dim3(kStatsChainThreads), 0, st,
+               reinterpret_cast<const __nv_bfloat16*>(X), convw, dil, m.L, m.C, n_kb, 1e-3f,
+               stats);
     };
     auto pick = [&](auto cp) {
       constexpr int CPc = decltype(cp)::value;
@@ -416,7 +438,7 @@ int launch_stats(const Dims& m, const act_t* X, const float* convw, int dil, int
     }
     return launch_status();
   }
-  return launch_stats_direct<act_t>(m, X, convw, dil, batch, stats, st);
+  return launch_stats_direct<act_t>(m, X, convw, dil, batch, stats, pdl, st);
 }
 
 // The whole forward for `batch` rows whose stem input is `in` (kind kIn).
@@ -425,13 +447,10 @@ int run_forward_t(const Dims& m, const PackLayout& pl, const uint8_t* packed, in
                   const StemInput& in, const float* x_ctl, float* profile, float* logcounts,
                   uint8_t* ws, cudaStream_t st) {
   const FwdLayout f = fwd_layout(m, batch);
-  unsigned* counters = reinterpret_cast<unsigned*>(ws + f.counters);
   float2* stats = reinterpret_cast<float2*>(ws + f.stats);
-  float* partials = reinterpret_cast<float*>(ws + f.partials);
   int* status = reinterpret_cast<int*>(ws + f.status);
   act_t* xa = reinterpret_cast<act_t*>(ws + f.xa);
   act_t* xb = reinterpret_cast<act_t*>(ws + f.xb);
-  if (cudaMemsetAsync(counters, 0, (size_t)batch * 4, st) != cudaSuccess) return CHM_ERR_CUDA;
 
   // stem (tcgen05 im2col GEMM)
   const long long rows = (long long)batch * m.L;
@@ -487,7 +506,7 @@ int run_forward_t(const Dims& m, const PackLayout& pl, const uint8_t* packed, in
     const uint8_t* lw = packed + pl.layers + pl.layer_stride * i;
     const float* convw = reinterpret_cast<const float*>(lw + pl.l_convw);
     const int dil = 1 << i;
-    CHM_TRY(launch_stats<act_t>(m, xa, convw, dil, batch, partials, counters, stats, status, st));
+    CHM_TRY(launch_stats<act_t>(m, xa, convw, dil, batch, stats, /*pdl=*/true, st));
     MlpArgs a;
     a.X_in = xa;
     a.X_out = xb;
@@ -530,7 +549,7 @@ int run_forward_t(const Dims& m, const PackLayout& pl, const uint8_t* packed, in
     LaunchTimer timer(kKProfile, st);
     auto go = [&](auto k) {
       cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, hd3::kAlloc);
-      k<<<hgrid, hd3::kThreads, hd3::kAlloc, st>>>(h, tmap);
+      launch_k(true, k, dim3(hgrid), dim3(hd3::kThreads), hd3::kAlloc, st, h, tmap);
     };
     if (m.CP == 128) go(head_fused_kernel<128>);
     else go(head_fused_kernel<256>);
@@ -661,16 +680,14 @@ bool block_supported(int C, int H) {
 }
 
 struct BlockWsLayout {
-  size_t status, counters, stats, partials, xin, xout, total;
+  size_t status, stats, xin, xout, total;
 };
 
 BlockWsLayout block_ws_layout(const Dims& m, int batch) {
   BlockWsLayout b;
   size_t o = 0;
   b.status = o; o = align_up(o + 256);
-  b.counters = o; o = align_up(o + (size_t)batch * 4);
   b.stats = o; o = align_up(o + (size_t)batch * 8);
-  b.partials = o; o = align_up(o + (size_t)batch * m.n_chunks() * 12);
   const size_t act = (m.C == m.CP) ? 0 : (size_t)batch * m.L * m.CP * m.act_bytes();
   b.xin = o; o = align_up(o + act);
   b.xout = o; o = align_up(o + act);
@@ -683,9 +700,7 @@ int run_block_t(const Dims& m, int batch, int dil, const uint8_t* packed, const 
                 act_t* out, uint8_t* ws, cudaStream_t st) {
   const BlockWsLayout bl = block_ws_layout(m, batch);
   const PackLayout pl = pack_layout(m);
-  unsigned* counters = reinterpret_cast<unsigned*>(ws + bl.counters);
   float2* stats = reinterpret_cast<float2*>(ws + bl.stats);
-  float* partials = reinterpret_cast<float*>(ws + bl.partials);
   const long long rows = (long long)batch * m.L;
   const act_t* xin = x;
   act_t* xout = out;
@@ -697,10 +712,8 @@ int run_block_t(const Dims& m, int batch, int dil, const uint8_t* packed, const 
     xin = pin;
     xout = reinterpret_cast<act_t*>(ws + bl.xout);
   }
-  if (cudaMemsetAsync(counters, 0, (size_t)batch * 4, st) != cudaSuccess) return CHM_ERR_CUDA;
   const float* convw = reinterpret_cast<const float*>(packed + pl.l_convw);
-  CHM_TRY(launch_stats<act_t>(m, xin, convw, dil, batch, partials, counters, stats,
-                              reinterpret_cast<int*>(ws + bl.status), st));
+  CHM_TRY(launch_stats<act_t>(m, xin, convw, dil, batch, stats, /*pdl=*/m.C != m.CP, st));
   const int n_tiles = static_cast<int>((rows + kTileRows - 1) / kTileRows);
   MlpArgs a;
   a.X_in = xin;

@@ -19,7 +19,6 @@ constexpr int kStemPad = 10;
 constexpr int kHeadTaps = 75;   // fconv kernel size (upstream cherimoya.py:182-184)
 constexpr int kHeadPad = 37;
 constexpr int kTileRows = 128;  // MMA M
-constexpr int kStatsRows = 128; // rows per LayerNorm-statistics partial
 
 enum : int { kStatusOk = 0, kStatusTimeout = 5 };
 
@@ -470,6 +469,7 @@ __global__ void __launch_bounds__(sm2::kThreads, 1) stem_tc_kernel(
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  griddep_wait();                          // the previous kernel's outputs are visible
   const uint32_t tmem = *slot + g * 128;
   const uint32_t sA_addr = smem_u32(sA), sB_addr = smem_u32(sB);
   const uint32_t idesc = idesc_bf16(kTileRows, 128);
@@ -612,6 +612,7 @@ __global__ void __launch_bounds__(kStats2Threads) stats_example_kernel(
     w2[j] = convw[2 * CP + c0 + j];
     if (c0 + j >= C) { w0[j] = 0.f; w1[j] = 0.f; w2[j] = 0.f; }
   }
+  griddep_wait();                          // the previous kernel's outputs are visible
   const act_t* Xb = X + (long long)b * L * CP + c0;
   double S = 0.0, Q = 0.0;
   constexpr int kU = sizeof(act_t) == 2 ? 4 : 2;   // rows in flight per thread
@@ -701,6 +702,7 @@ __global__ void __launch_bounds__(kStatsChainThreads, 2) stats_chain_kernel(
     w1[m] = f2{c < C ? convw[CP + c] : 0.f, c + 1 < C ? convw[CP + c + 1] : 0.f};
     w2[m] = f2{c < C ? convw[2 * CP + c] : 0.f, c + 1 < C ? convw[2 * CP + c + 1] : 0.f};
   }
+  griddep_wait();                          // the previous kernel's outputs are visible
   const uint4* Xb = reinterpret_cast<const uint4*>(X + (size_t)b * L * CP) + ch;
   const int n_seg = dil * n_kb;
   double S = 0.0, Q = 0.0;
@@ -1285,6 +1287,7 @@ __global__ void __launch_bounds__(wd::kThreads, 1) mlp_wide_kernel(MlpArgs a) {
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  griddep_wait();                          // the previous kernel's outputs are visible
   const uint32_t tmem = *slot;
   const int n_my = (a.n_tiles > static_cast<int>(blockIdx.x))
                        ? (a.n_tiles - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
@@ -1696,6 +1699,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  griddep_wait();                          // the previous kernel's outputs are visible
   const uint32_t tmem = *slot;
   const int first = blockIdx.x;
   const int stride = gridDim.x;
@@ -2620,6 +2624,7 @@ __global__ void __launch_bounds__(hd3::kThreads, 1) head_fused_kernel(
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  griddep_wait();                          // the previous kernel's outputs are visible
   const uint32_t tmem = *slot;
   auto item_of = [&](int g, int& b, int& o, int& k) {
     const int i = g / n_tiles;

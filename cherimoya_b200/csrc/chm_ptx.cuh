@@ -15,6 +15,16 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// ---------------------------------------------------------------- launches
+// Kernels launched with programmatic stream serialization may start while the
+// previous kernel of the stream finishes; this waits until it has completed
+// and its memory is visible. Everything before it may only touch this
+// kernel's own shared memory / TMEM and data no earlier kernel of the same
+// call writes.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
