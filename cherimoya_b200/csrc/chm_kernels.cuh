@@ -2552,14 +2552,16 @@ __global__ void __launch_bounds__(hd::kThreads) head_kernel(HeadArgs a) {
 // count head rides in the same MMA: the five spare operand rows after the 75
 // taps hold the count Linear's weights (output 0 only), so Z[w, 75 + g] =
 // sum_c X[w, c] lw[g, c] and logcount[g] = lbias[g] + sum_w Z[w, 75 + g] / Lout
-// over the trimmed window. Diagonal sums of the profile are split over two
+// over the trimmed window. Diagonal sums of the profile are split over four
 // threads per output and combined in a fixed order (deterministic).
-// Warps 0-7 run the epilogue (Z -> ring -> diagonal sums -> profile); warp 8
+// Warps 0-15 run the epilogue (Z -> ring -> diagonal sums -> profile); warp 16
 // issues the TMA loads and the MMAs, so Z of the next tile is computed while
 // the epilogue works on the current one (two TMEM buffers).
 namespace hd3 {
-constexpr int kEpiThreads = 256;
+constexpr int kEpiThreads = 512;
 constexpr int kIssuerWarp = kEpiThreads / 32;
+constexpr int kTapParts = kEpiThreads / 128;             // threads per output's diagonal
+static_assert(kTapParts == 4, "the profile store sums four tap parts");
 constexpr int kThreads = kEpiThreads + 32;
 constexpr int kABufs = 3;
 constexpr int kMaxGroups = hd::kNP - kHeadTaps;          // 5 spare operand rows
@@ -2568,7 +2570,7 @@ constexpr uint32_t kB = 0;                               // F hi | lo: 2 x 80 x 
 constexpr uint32_t kA = 40960;                           // kABufs x 2 boxes
 constexpr uint32_t kRingOff = kA + kABufs * 2 * kBox;
 constexpr uint32_t kPart = kRingOff + hd::kRing * hd::kZStride * 4;
-constexpr uint32_t kRed = kPart + 2 * 128 * 4;
+constexpr uint32_t kRed = kPart + kTapParts * 128 * 4;
 constexpr uint32_t kBars = kRed + 8 * kMaxGroups * 4 + 32;
 constexpr int kNumBars = 2 * kABufs + 5;  // a_full[3] z_full[2] z_free[2] mma_done a_free[3]
 constexpr uint32_t kSlot = kBars + kNumBars * 8;
@@ -2724,45 +2726,45 @@ __global__ void __launch_bounds__(hd3::kThreads, 1) head_fused_kernel(
       ok = mbar_wait(&z_full[zb], (g >> 1) & 1);
       if (!ok) break;
       tc_fence_after();
-      // ---- Z tile -> ring rows (128 k + w) mod kRing; count columns 75..79
+      // ---- Z tile -> ring rows (128 k + w) mod kRing; column group cg of the
+      // warp: [0, 32), [32, 64), [64, 80) (taps 64..74 and the count columns);
+      // group 3 has no columns
+      const int cg = warp >> 2;
       {
         float* zrow = ring + ((k * kTileRows + w) % kRing) * kZStride;
-        uint32_t r[32];
-        if (warp < 4) {
-#pragma unroll 1
-          for (int part_c = 0; part_c < 2; ++part_c) {
-            tmem_ld32(tmem + zb * 128 + lane_sel + part_c * 32, r);
+        if (cg < 2) {
+          uint32_t r[32];
+          tmem_ld32(tmem + zb * 128 + lane_sel + cg * 32, r);
 #pragma unroll
-            for (int q = 0; q < 32; ++q) zrow[part_c * 32 + q] = __uint_as_float(r[q]);
-          }
-        } else {
-          tmem_ld32(tmem + zb * 128 + lane_sel + 48, r);   // columns 48..79
+          for (int q = 0; q < 32; ++q) zrow[cg * 32 + q] = __uint_as_float(r[q]);
+        } else if (cg == 2) {
+          uint32_t r[16];
+          tmem_ld16(tmem + zb * 128 + lane_sel + 64, r);   // columns 64..79
 #pragma unroll
-          for (int q = 16; q < 32; ++q) {
-            const int t = 48 + q;
-            if (t < kHeadTaps) zrow[t] = __uint_as_float(r[q]);
-          }
+          for (int q = 0; q < kHeadTaps - 64; ++q) zrow[64 + q] = __uint_as_float(r[q]);
           const int wr = k * kTileRows + w;                // window row
           if (o == 0 && wr >= kHeadPad && wr < kHeadPad + a.Lout) {
 #pragma unroll
             for (int gi = 0; gi < hd3::kMaxGroups; ++gi)
-              cnt[gi] += __uint_as_float(r[kHeadTaps - 48 + gi]);
+              cnt[gi] += __uint_as_float(r[kHeadTaps - 64 + gi]);
           }
         }
       }
       tc_fence_before();
       mbar_arrive_warp(&z_free[zb]);                      // TMEM buffer zb is free again
       named_sync(1, hd3::kEpiThreads);
-      // ---- diagonal sums: output j = sum_t ring[(j + t) mod kRing][t], two halves
+      // ---- diagonal sums: output j = sum_t ring[(j + t) mod kRing][t], in
+      // kTapParts tap ranges
       const int j_lo = (k == 0) ? 0 : k * kTileRows - (kHeadTaps - 1);
       const int j_hi = (k == n_tiles - 1) ? a.Lout
                                           : min(a.Lout, k * kTileRows + kTileRows - (kHeadTaps - 1));
       {
-        const int jj = tid & 127, half = tid >> 7;
+        const int jj = tid & 127, tp = tid >> 7;
         const int j = j_lo + jj;
         if (j < j_hi) {
-          const int t0 = half ? 38 : 0, t1 = half ? kHeadTaps : 38;
-          part[half * 128 + jj] = ring_diag_sum(ring, (j + t0) % kRing, t0, t1 - t0);
+          const int t0 = (tp * kHeadTaps) / hd3::kTapParts;
+          const int t1 = ((tp + 1) * kHeadTaps) / hd3::kTapParts;
+          part[tp * 128 + jj] = ring_diag_sum(ring, (j + t0) % kRing, t0, t1 - t0);
         }
       }
       named_sync(1, hd3::kEpiThreads);
@@ -2770,17 +2772,17 @@ __global__ void __launch_bounds__(hd3::kThreads, 1) head_fused_kernel(
         const int j = j_lo + tid;
         if (j < j_hi)
           a.profile[((long long)b * a.n_out + o) * a.Lout + j] =
-              (part[tid] + part[128 + tid]) + a.fbias[o];
+              ((part[tid] + part[128 + tid]) + (part[256 + tid] + part[384 + tid])) + a.fbias[o];
       }
       // ---- count head at the end of an item of output 0: fixed-order reduction
       if (o == 0 && k == n_tiles - 1) {
-        if (warp >= 4) {
+        if (cg == 2) {
 #pragma unroll
           for (int gi = 0; gi < hd3::kMaxGroups; ++gi) {
             float v = cnt[gi];
 #pragma unroll
             for (int sh = 16; sh > 0; sh >>= 1) v += __shfl_xor_sync(0xffffffffu, v, sh);
-            if (lane == 0) red[(warp - 4) * hd3::kMaxGroups + gi] = v;
+            if (lane == 0) red[(warp - 8) * hd3::kMaxGroups + gi] = v;
             cnt[gi] = 0.f;
           }
         }
