@@ -1704,6 +1704,10 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
   const int first = blockIdx.x;
   const int stride = gridDim.x;
   const int n_my = (a.n_tiles > first) ? (a.n_tiles - first + stride - 1) / stride : 0;
+  // tiles run from the last example to the first: the statistics kernel just
+  // read the last examples (still in L2), and the next one starts at the first
+  // examples, which this launch writes last
+  auto tile_of = [&](int tit) -> int { return a.n_tiles - 1 - (first + tit * stride); };
 
   if (warp < kProducerWarps) {
     // ------------------------------------------------------------ producer
@@ -1715,11 +1719,11 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
     // tiles are per example: tile -> (example n, first position l0); rows
     // outside [0, L) of the example arrive as zero from the 3-D tensor map,
     // which is the conv's zero padding, so no row needs a mask
-    float2 st_next = (n_my > 0) ? a.stats[first / a.tpe] : make_float2(0.f, 0.f);
+    float2 st_next = (n_my > 0) ? a.stats[tile_of(0) / a.tpe] : make_float2(0.f, 0.f);
     for (int it = 0; it < n_my && ok; ++it) {
       const int buf = it & 1;
       const float2 st = st_next;                   // statistics loaded one tile ahead
-      if (it + 1 < n_my) st_next = a.stats[(first + (it + 1) * stride) / a.tpe];
+      if (it + 1 < n_my) st_next = a.stats[tile_of(it + 1) / a.tpe];
       const f2 scale2{st.y, st.y};
       const f2 shift2{-st.x * st.y, -st.x * st.y};
       // bf16 fast path: A1 carries a factor 1/2 (exact), which the GELU of
@@ -1944,7 +1948,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
         // after the previous tile's store left the buffer)
         const bool leader = (warp == kResidualWarp0 && lane == 0);
         auto load_res = [&](int tit) {
-          const int tile = first + tit * stride;
+          const int tile = tile_of(tit);
           const int n = tile / a.tpe, l0 = (tile - n * a.tpe) * kTileRows;
           mbar_expect_tx(&bars[RES_FULL], 2 * kResBox);
           tma_load_3d(sRes, &maps.res, 0, l0, n, &bars[RES_FULL]);
@@ -1983,7 +1987,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
         mbar_arrive_warp(&bars[RES_DONE]);
         if (leader) {
           if (!mbar_wait_abortable(&bars[RES_DONE], it & 1, abort_flag)) break;
-          const int tile = first + it * stride;
+          const int tile = tile_of(it);
           const int n = tile / a.tpe, l0 = (tile - n * a.tpe) * kTileRows;
           tma_store_3d(&maps.out, sRes, 0, l0, n);        // rows past L are clipped
           tma_store_3d(&maps.out, sRes + kResBox, 64, l0, n);
@@ -1997,7 +2001,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
         }
       } else {
         // residual of D2 on rows read directly from global memory (fp32)
-        const int tile = first + it * stride;
+        const int tile = tile_of(it);
         const int n = tile / a.tpe, l = (tile - n * a.tpe) * kTileRows + rl;
         const bool rv = l < a.L;
         const long long r = (long long)n * a.L + l;
@@ -2118,7 +2122,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       auto issue = [&](uint32_t k, uint32_t slotk) {
         const int tit = static_cast<int>(k / kBoxes);
         const int b = static_cast<int>(k % kBoxes);
-        const int tile = first + tit * stride;
+        const int tile = tile_of(tit);
         const int n = tile / a.tpe, l0 = (tile - n * a.tpe) * kTileRows;
         if constexpr (kWide) {
           // one block of rows [l0 - d, l0 - d + wide_rows(d)) (the map's box)
