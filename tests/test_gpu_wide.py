@@ -113,3 +113,23 @@ def test_expansion3_streamed_mlp_against_oracle(mode):
     m.precision = mode
     p, c = _engine(m.cuda(), X)
     _check(mode, p, c, rp, rc, "expansion 3")
+
+
+@pytest.mark.parametrize("mode", ["fp32", "bf16"])
+@pytest.mark.parametrize("n_filters,expansion", [(256, 1), (200, 2)])
+def test_wide_widths_against_oracle(mode, n_filters, expansion):
+    """n_filters 256 with expansion 1 (four hidden chunks in the streamed-weight
+    kernel) and n_filters 200 (padded to 256 channels: the padded channels must
+    stay zero through the stem halves, the MLP and the 256-wide head)."""
+    torch.manual_seed(7)
+    m = cb.Cherimoya(n_filters=n_filters, n_layers=3, expansion=expansion, trimming=300,
+                     compile=False).eval()
+    sd = {k: v.float() for k, v in m.state_dict().items()}
+    cfg = {"n_layers": 3, "residual_scale": 0.15, "trimming": 300}
+    g = torch.Generator().manual_seed(8)
+    X = O.one_hot(torch.randint(0, 4, (3, 1300), generator=g))
+    with torch.no_grad():
+        rp, rc = O.forward(sd, cfg, X)
+    m.precision = mode
+    p, c = _engine(m.cuda(), X)
+    _check(mode, p, c, rp, rc, "n_filters %d expansion %d" % (n_filters, expansion))
