@@ -46,7 +46,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "seqs/sec fwd (2114bp, 9-layer) & ISM mutants/sec at 1/2/4/8 B200; % roofline"
-MLP_DRAM_BYTES_PER_SEQ = (138.728704e6 + 94.934528e6) / 256   # measured, bf16 mode
+MLP_DRAM_BYTES_PER_SEQ = (138.766592e6 + 93.712896e6) / 256   # measured, bf16 mode
 L = 2114
 WORKLOADS = {
     # name: (model kwargs, default batch per GPU, input seed base, unit)
@@ -454,7 +454,7 @@ def run_ours(args, world, rank, local):
         "frac_of_burst": achieved / peaks["bf16_tflops"],
         # DRAM bytes of one MLP launch of the default-width backbone: ncu
         # dram__bytes_read.sum + write.sum of the layer-0 launch at batch 256
-        # (138.73 MB + 94.93 MB), scaled by the sequences processed
+        # (138.77 MB + 93.71 MB), scaled by the sequences processed
         "traffic": (MLP_DRAM_BYTES_PER_SEQ * args.batch
                     if args.mode == "bf16" and default_width and not variant else None),
         "traffic_unit": "bytes per launch",
