@@ -479,6 +479,32 @@ int run_forward_t(const Dims& m, const PackLayout& pl, const uint8_t* packed, in
         else go(stem_tc_kernel<kInIsm, 1>);
         CHM_TRY(launch_status());
       }
+    } else if (sizeof(act_t) == 4 && (m.CP == 128 || m.CP == 256)) {
+      // fp32 mode: the same tcgen05 stem with an fp32 output tile (two
+      // warpgroups per CTA); dense fp32 input as bf16 hi + lo (three MMA terms)
+      CUtensorMap tmap;
+      CHM_TRY(make_act_tmap3_box(&tmap, xa, batch, m.L, m.CP, 4, 128, kTileRows));
+      const int tiles = batch * ((m.L + kTileRows - 1) / kTileRows);
+      constexpr int kG = sm2::groups_for(4);
+      const int tgrid = std::max(1, std::min((tiles + kG - 1) / kG, device_sms()));
+      const int splits = split ? 2 : 1;
+      const int tsmem = static_cast<int>(sm2::smem_bytes(splits, 4));
+      for (int c_off = 0; c_off < m.CP; c_off += 128) {
+        auto go = [&](auto k) {
+          cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, tsmem);
+          k<<<tgrid, 128 * kG, tsmem, st>>>(in, wpk, bias, tmap, batch, m.L, m.C, m.CP, c_off,
+                                            tiles, status);
+        };
+        if (kIn == kInDense) {
+          if (split) go(stem_tc_kernel<kInDense, 2, float>);
+          else go(stem_tc_kernel<kInDense, 1, float>);
+        } else if (kIn == kInBases) {
+          go(stem_tc_kernel<kInBases, 1, float>);
+        } else {
+          go(stem_tc_kernel<kInIsm, 1, float>);
+        }
+        CHM_TRY(launch_status());
+      }
     } else {
     const int smem = stem_smem_bytes(m.CP, split ? 2 : 1);
     const int sgrid = std::min(n_tiles, 2 * device_sms());

@@ -404,19 +404,27 @@ constexpr uint32_t kA = kTileRows * sm::kK * 2;    // 32 KB
 __host__ __device__ constexpr uint32_t cols_bytes(int a_splits) {
   return static_cast<uint32_t>(a_splits * kCols * 8);
 }
-// [W hi|lo][A group 0..3][cols 0..3][bias][barriers]: every swizzled operand /
+// bf16 output: four warpgroups, A buffer of a_splits x 32 KB each; fp32
+// output: two warpgroups, each A region 64 KB (it also holds the fp32 output
+// tile, four 32-channel boxes)
+__host__ __device__ constexpr int groups_for(int out_bytes) { return out_bytes == 4 ? 2 : kGroups; }
+__host__ __device__ constexpr int a_alloc(int a_splits, int out_bytes) {
+  return out_bytes == 4 ? 2 : a_splits;
+}
+// [W hi|lo][A group 0..][cols 0..][bias][barriers]: every swizzled operand /
 // TMA box starts on a 1024-byte boundary
-__host__ __device__ constexpr uint32_t cols_off(int a_splits) {
-  return kW + kGroups * a_splits * kA;
+__host__ __device__ constexpr uint32_t cols_off(int a_splits, int out_bytes = 2) {
+  return kW + groups_for(out_bytes) * a_alloc(a_splits, out_bytes) * kA;
 }
 __host__ __device__ constexpr uint32_t cols_stride(int a_splits) {
   return (cols_bytes(a_splits) + 127) & ~127u;
 }
-__host__ __device__ constexpr uint32_t smem_bytes(int a_splits) {
-  return cols_off(a_splits) + kGroups * cols_stride(a_splits) + 128 * 4 + 8 * kGroups + 16 +
-         1024;
+__host__ __device__ constexpr uint32_t smem_bytes(int a_splits, int out_bytes = 2) {
+  return cols_off(a_splits, out_bytes) + groups_for(out_bytes) * cols_stride(a_splits) +
+         128 * 4 + 8 * groups_for(out_bytes) + 16 + 1024;
 }
 static_assert(smem_bytes(1) <= 232448, "shared memory per block");
+static_assert(smem_bytes(2, 4) <= 232448, "shared memory per block (fp32 output)");
 static_assert(kW % 1024 == 0 && kA % 1024 == 0, "swizzled buffers need 1024-byte alignment");
 }  // namespace sm2
 
@@ -427,28 +435,33 @@ __device__ __forceinline__ uint2 bf16x4_hi(const float (&v)[4]) {
 // Output channels [c_off, c_off + 128) of a model with CP padded channels
 // (CP = 128: one launch; CP = 256: two, c_off = 0 and 128). wpk is the packed
 // [hi | lo] weight with CP rows per 128-byte-swizzled K box.
-template <int kIn, int kASplits>
+// out_t = float (fp32 mode): two warpgroups, exact GELU, the fp32 tile stored
+// as four 32-channel boxes.
+template <int kIn, int kASplits, typename out_t = __nv_bfloat16>
 __global__ void __launch_bounds__(sm2::kThreads, 1) stem_tc_kernel(
     StemInput in, const uint8_t* __restrict__ wpk, const float* __restrict__ bias,
     const __grid_constant__ CUtensorMap tmap, int batch, int L, int C, int CP, int c_off,
     int n_tiles, int* status) {
   using namespace sm2;
+  constexpr bool kF32 = sizeof(out_t) == 4;
+  constexpr int kG = groups_for(sizeof(out_t));             // warpgroups
+  constexpr int kAA = a_alloc(kASplits, sizeof(out_t));     // 32 KB A buffers per group
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int tid = threadIdx.x, warp = tid >> 5;
   const int g = tid >> 7, gt = tid & 127;            // warpgroup, row within the tile
   uint8_t* sB = smem;
-  uint8_t* sA = smem + kW + g * kASplits * kA;       // [kASplits] 128 x 128 bf16
-  uint2* cols = reinterpret_cast<uint2*>(smem + cols_off(kASplits) +
+  uint8_t* sA = smem + kW + g * kAA * kA;            // [kASplits] 128 x 128 bf16
+  uint2* cols = reinterpret_cast<uint2*>(smem + cols_off(kASplits, sizeof(out_t)) +
                                          g * cols_stride(kASplits));   // [kASplits][kCols]
-  float* sbias =
-      reinterpret_cast<float*>(smem + cols_off(kASplits) + kGroups * cols_stride(kASplits));
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sbias + 128);    // [kGroups]
-  uint32_t* slot = reinterpret_cast<uint32_t*>(bar + kGroups);
-  if (warp == 0) tmem_alloc(slot, 128 * kGroups);
+  float* sbias = reinterpret_cast<float*>(smem + cols_off(kASplits, sizeof(out_t)) +
+                                          kG * cols_stride(kASplits));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sbias + 128);    // [kG]
+  uint32_t* slot = reinterpret_cast<uint32_t*>(bar + kG);
+  if (warp == 0) tmem_alloc(slot, 128 * kG);
   if (tid == 0) {
-    for (int i = 0; i < kGroups; ++i) mbar_init(&bar[i], 1);
+    for (int i = 0; i < kG; ++i) mbar_init(&bar[i], 1);
     mbar_init_fence();
   }
   {
@@ -478,7 +491,7 @@ __global__ void __launch_bounds__(sm2::kThreads, 1) stem_tc_kernel(
   const uint32_t bar_id = 1 + g;
   uint32_t it = 0;
   bool ok = true;
-  for (int tile = blockIdx.x * kGroups + g; tile < n_tiles; tile += gridDim.x * kGroups, ++it) {
+  for (int tile = blockIdx.x * kG + g; tile < n_tiles; tile += gridDim.x * kG, ++it) {
     const int b = tile / tpe;
     const int l0 = (tile - b * tpe) * kTileRows;
     // ---- stage input columns l0 - 10 .. l0 + 137 (zero outside [0, L))
@@ -542,6 +555,32 @@ __global__ void __launch_bounds__(sm2::kThreads, 1) stem_tc_kernel(
       break;
     }
     tc_fence_after();
+    if constexpr (kF32) {
+      // ---- GELU -> fp32 output tile in sA: four 32-channel boxes (128-byte
+      // rows, 128-byte swizzle), box j = channels [32 j, 32 j + 32)
+#pragma unroll 1
+      for (int j = 0; j < 4; ++j) {
+        uint32_t d[32];
+        tmem_ld32(tmem + lane_sel + j * 32, d);
+        uint8_t* box = sA + j * kA / 2;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float y[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) y[e] = gelu_tanh<false>(__uint_as_float(d[4 * q + e]));
+          *reinterpret_cast<float4*>(box + gt * 128 + ((q ^ (gt & 7)) << 4)) =
+              make_float4(y[0], y[1], y[2], y[3]);
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      named_sync(bar_id, 128);
+      if (gt == 0) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) tma_store_3d(&tmap, sA + j * kA / 2, c_off + 32 * j, l0, b);
+        bulk_commit();
+      }
+    } else {
     // ---- bias + GELU -> bf16 output tile in sA (two 64-channel boxes)
 #pragma unroll 1
     for (int j = 0; j < 4; ++j) {
@@ -569,13 +608,14 @@ __global__ void __launch_bounds__(sm2::kThreads, 1) stem_tc_kernel(
       tma_store_3d(&tmap, sA + kTileRows * 128, c_off + 64, l0, b);
       bulk_commit();
     }
+    }
   }
   if (gt == 0) bulk_wait0();
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(*slot, 128 * kGroups);
+    tmem_dealloc(*slot, 128 * kG);
   }
 }
 
