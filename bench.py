@@ -117,6 +117,17 @@ class ClockSampler:
             self.proc.wait(5)
         except Exception:
             self.proc.kill()
+        if not self.lines:
+            # a timed region shorter than the sampling interval: one reading
+            # taken right after it
+            try:
+                out = subprocess.run(
+                    ["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.QUERY,
+                     "--format=csv,noheader,nounits"],
+                    capture_output=True, text=True, timeout=20).stdout
+                self.lines = [ln.strip() for ln in out.splitlines() if ln.strip()]
+            except Exception:
+                pass
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines:
