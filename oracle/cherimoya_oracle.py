@@ -197,7 +197,7 @@ def ism_scores(sd, config, bases, start, end, batch=256):
 
     For sequence n, position p and base b the mutant is the reference with
     base b at p (b equal to the reference base reproduces the reference).
-    Scores, per BASELINE's ISM definition and the upstream metric:
+    Scores, following the upstream ISM metric:
       d_logcount[n, b, p-start] = logcount(mutant)[0] - logcount(ref)[0]
       jsd[n, b, p-start] = jensen_shannon_distance(profile(mutant) flattened,
                                                    softmax(profile(ref)) flattened)

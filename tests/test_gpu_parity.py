@@ -5,7 +5,7 @@ Every test here runs the CUDA path through the C-ABI library
 the upstream package (tests/golden) or with the CPU oracle on the same
 seeded inputs and the same state_dict.
 
-Tolerances (BASELINE north star):
+Tolerances:
   fp32 mode: max abs error <= 1e-4 on profile logits and log-counts
   bf16 mode: max abs error <= 1e-2 and per-track profile Pearson >= 0.9999
 """
