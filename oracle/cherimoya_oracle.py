@@ -242,3 +242,16 @@ def variant_scores(sd, config, ref_bases, alt_bases):
     pr = torch.softmax(p_r.reshape(N, -1), dim=-1)
     j = jensen_shannon_distance(p_a.reshape(N, -1), pr)
     return c_a - c_r, j
+
+
+def reverse_complement_average(sd, config, X, X_ctl=None):
+    """Forward / reverse-complement averaging of the upstream evaluate command
+    (cherimoya_cli/commands/evaluate.py:80-96): the reverse complement flips
+    the base and position axes of X (and of X_ctl), its profile is flipped
+    back over channels and positions, and both outputs are averaged with the
+    forward strand's."""
+    with torch.no_grad():
+        p, c = forward(sd, config, X, X_ctl)
+        p_rc, c_rc = forward(sd, config, torch.flip(X, dims=(-1, -2)),
+                             None if X_ctl is None else torch.flip(X_ctl, dims=(-1, -2)))
+    return (p + torch.flip(p_rc, dims=(-1, -2))) / 2, (c + c_rc) / 2
