@@ -69,10 +69,11 @@ def predict(model, X, args=None, batch_size=64, device="cuda", dtype="float32", 
 
     X: (N, 4, L) tensor on the host or on ``device``; args: None or a tuple
     of per-example tensors passed after X (control tracks). Returns the
-    model's outputs concatenated over batches as host tensors: a tuple when
-    the model returns a tuple, else one tensor. With
-    ``reverse_complement_average`` the model must return (profile,
-    logcounts) and both strands are averaged (``rc_forward``).
+    model's outputs concatenated over batches as host tensors (in pinned
+    memory when ``device`` is a GPU): a tuple when the model returns a
+    tuple, else one tensor. With ``reverse_complement_average`` the model
+    must return (profile, logcounts) and both strands are averaged
+    (``rc_forward``).
     """
     extra = tuple(args) if args is not None else ()
     for a in extra:
@@ -124,7 +125,8 @@ def _predict_cuda(model, X, extra, batches, dev, rc, progress):
     else:
         srcs = tuple(t.contiguous() for t in srcs)
         on_dev = [t.device == dev for t in srcs]
-        pinned = [d or t.is_pinned() for t, d in zip(srcs, on_dev)]
+        # inputs on another GPU copy device to device, without host staging
+        pinned = [d or t.is_cuda or t.is_pinned() for t, d in zip(srcs, on_dev)]
         # two device buffers (and, for pageable host inputs, two pinned host
         # buffers) per input not already on the device, used by alternate batches
         dbuf = [[None if d else torch.empty((bmax,) + tuple(t.shape[1:]), dtype=t.dtype,
