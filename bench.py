@@ -12,15 +12,20 @@ mode (bf16 residual stream, fp32 LayerNorm statistics and accumulation).
 N > 1 runs under torchrun, one rank per GPU, each rank its own batch
 (weak scaling, no collective on the data path). Prints one JSON line on
 rank 0. `value` = sequences/s of the whole job with inputs resident in
-HBM; `e2e` = the same through the public API (`model(X)`) with host
-inputs copied in and outputs copied out inside the timed region; `ism` =
-on-device saturation-mutagenesis mutants/s; `roofline` = the MLP kernel's
-achieved tensor FLOP/s over the measured bf16 peak; `cpu_baseline` = the
-oracle (the upstream PyTorch CPU path restated) on the host cores.
+HBM, timed without per-kernel instrumentation; `e2e` = the same through
+the public API (`model(X)`) with host inputs copied in and outputs copied
+out inside the timed region; `ism` = saturation mutagenesis of 256
+sequences x all 3 x 2114 substitutions, sharded over the ranks, with the
+H2D copy of the bases and the all-gather + D2H of the scores inside the
+timed region (mutants/s); `roofline` = the dominant kernel's achieved
+tensor FLOP/s over the measured burst bf16 peak (a millisecond-long
+step), with the whole forward's fraction beside it; `cpu_baseline` = the
+upstream package's CPU forward on the host cores.
 
---impl reference times the upstream algorithm's CPU implementation (the
-oracle port) on the same workload, a bounded sample of sequences per step,
-on rank 0 only.
+--impl reference times the upstream package's own CPU forward (the
+reference's pure-PyTorch path, imported from baseline/_ref by
+oracle/upstream.py; the oracle port when that install is absent) on the
+same workload, a bounded sample of sequences per step, on rank 0 only.
 
 --workload selects the model and input set (the default is the one above):
   forward    default 9-layer model, uniform random sequences, batch 1024
@@ -68,6 +73,10 @@ def flop_per_seq(model):
 
 def mlp_flop_per_seq(model):
     return 4 * model.n_filters * model.n_filters * model.expansion * L * model.n_layers
+
+
+REF_WHAT = {"reference": "upstream cherimoya 0.2.1 Cherimoya.forward (baseline/_ref)",
+            "port": "oracle restatement of the upstream CPU path"}
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -212,29 +221,50 @@ def build_model(args):
     return cb.Cherimoya(compile=False, precision=args.mode, **WORKLOADS[args.workload][0])
 
 
-def oracle_step(args, n):
-    """The oracle's (upstream PyTorch CPU path restated) fp32 work for n units
-    of the workload: a callable running it once."""
+def reference_step(args, n):
+    """The reference's fp32 CPU work for n units of the workload: (a callable
+    running it once, kind). kind "reference": the upstream package itself
+    (eager ``Cherimoya.forward`` under no_grad, compile=False; upstream
+    cherimoya/cherimoya.py:340-400 with cheri.py:84-98 for the blocks),
+    loaded with the same state_dict as the engine's model; kind "port": the
+    oracle's restatement, when no upstream install is present."""
     import torch
     from oracle import cherimoya_oracle as O
+    from oracle import upstream
     m = build_model(args)
     sd = {k: v.detach().float().clone() for k, v in m.state_dict().items()}
     cfg = m._init_kwargs()
     seed = WORKLOADS[args.workload][2]
     inputs = make_bases(args.workload, n, seed)
+    if upstream.available():
+        ref = upstream.import_upstream()
+        um = ref.Cherimoya(**cfg, compile=False).eval()
+        um.load_state_dict(sd)
+        if args.workload == "variant":
+            Xr, Xa = O.one_hot(inputs[0]), O.one_hot(inputs[1])
+
+            def run_pairs():
+                p_r, c_r = um(Xr)
+                p_a, c_a = um(Xa)
+                pr = torch.softmax(p_r.reshape(n, -1), dim=-1)
+                return c_a - c_r, ref.performance.jensen_shannon_distance(
+                    p_a.reshape(n, -1), pr)
+            return run_pairs, "reference"
+        X = O.one_hot(inputs[0])
+        return (lambda: um(X)), "reference"
     if args.workload == "variant":
-        return lambda: O.variant_scores(sd, cfg, inputs[0], inputs[1])
+        return (lambda: O.variant_scores(sd, cfg, inputs[0], inputs[1])), "port"
     X = O.one_hot(inputs[0])
-    return lambda: O.forward(sd, cfg, X)
+    return (lambda: O.forward(sd, cfg, X)), "port"
 
 
 def cpu_forward_rate(args, n_units, min_seconds=10.0, max_reps=8):
-    """Oracle fp32 rate on the host cores, units/s over a bounded sample of
-    n_units units (sequences, or pairs for the variant workload)."""
+    """Reference fp32 rate on the host cores, units/s over a bounded sample
+    of n_units units (sequences, or pairs for the variant workload)."""
     import torch
     cores = len(os.sched_getaffinity(0))
     torch.set_num_threads(cores)
-    run = oracle_step(args, n_units)
+    run, kind = reference_step(args, n_units)
     with torch.no_grad():
         run()                                       # warm-up
         times, t_all = [], time.perf_counter()
@@ -244,18 +274,18 @@ def cpu_forward_rate(args, n_units, min_seconds=10.0, max_reps=8):
             times.append(time.perf_counter() - t0)
             if time.perf_counter() - t_all >= min_seconds and len(times) >= 2:
                 break
-    return n_units / statistics.median(times), cores, len(times)
+    return n_units / statistics.median(times), cores, len(times), kind
 
 
 def run_reference(args, world, rank):
-    """--impl reference: the upstream algorithm's CPU path (oracle port)."""
+    """--impl reference: the upstream package's CPU path on the host cores."""
     if rank != 0:
         return
     import torch
     cores = len(os.sched_getaffinity(0))
     torch.set_num_threads(cores)
     sample = args.ref_sample
-    run = oracle_step(args, sample)
+    run, kind = reference_step(args, sample)
     unit = WORKLOADS[args.workload][3]
     with torch.no_grad():
         for _ in range(args.warmup):
@@ -271,9 +301,9 @@ def run_reference(args, world, rank):
         "ms_per_step": 1000.0 * dt / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": workload_config(args, world),
-        "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": "port",
-                         "sample": "{} of the batch's {} per step, fp32 eager "
-                                   "no_grad".format(sample, unit.split("/")[0])},
+        "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": kind,
+                         "sample": "{} of the batch's {} per step, fp32 eager no_grad, "
+                                   "{}".format(sample, unit.split("/")[0], REF_WHAT[kind])},
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -339,22 +369,36 @@ def run_ours(args, world, rank, local):
         barrier(world)
         torch.cuda.synchronize()
         sampler.start()
-        _lib.timing_collect()
-        _lib.timing_enable(True)
         for k in range(args.steps):
             flush.zero_()
             starts[k].record()
             step(dev_in)
             ends[k].record()
         torch.cuda.synchronize()
-        _lib.timing_enable(False)
         barrier(world)
         clocks = sampler.stop()
-        per_class = _lib.timing_collect()
         step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
         dev_ms = sum(step_ms)
         dev_ms_max = max_over_ranks(dev_ms, world, dev)
         value = world * args.batch * args.steps / (dev_ms_max / 1000.0)
+
+        # ---- per-kernel shares: a separate instrumented pass (CUDA events
+        # around every launch, on the launching stream), never the headline
+        n_inst = max(1, min(args.steps, 5))
+        _lib.timing_collect()
+        _lib.timing_enable(True)
+        inst_ms = 0.0
+        for _ in range(n_inst):
+            flush.zero_()
+            i0 = torch.cuda.Event(enable_timing=True)
+            i1 = torch.cuda.Event(enable_timing=True)
+            i0.record()
+            step(dev_in)
+            i1.record()
+            torch.cuda.synchronize()
+            inst_ms += i0.elapsed_time(i1)
+        _lib.timing_enable(False)
+        per_class = _lib.timing_collect()
 
         # ---- end to end through the public API, host buffers: every step copies
         # its one-hot inputs from pinned host memory and reads its outputs back.
@@ -421,37 +465,61 @@ def run_ours(args, world, rank, local):
                    "api": api + " on pinned host one-hot fp32 input; the next step's "
                                 "H2D copy overlaps the current step"}
 
-        # ---- saturation mutagenesis (sharded by sequence, weak scaling)
+        # ---- saturation mutagenesis: 256 sequences x all 3 x 2114 single-base
+        # substitutions (1,623,552 mutants), the sequences split into contiguous
+        # shards over the ranks. Timed per rank from the H2D copy of its shard's
+        # bases (pinned host int8) through the all-gather of every rank's scores
+        # and their D2H copy into pinned host memory on rank 0.
         ism = None
         if args.ism_seqs > 0 and args.workload == "forward":
-            bases = torch.randint(0, 4, (args.ism_seqs, L),
-                                  generator=torch.Generator().manual_seed(100 + rank))
-            bases = bases.to(torch.int8).to(dev)
-            cb.saturation_mutagenesis(model, bases[:1], 1000, 1010)     # warm-up
+            from cherimoya_b200.ism import gather_shards, shard_range
+            n_seq = args.ism_seqs
+            all_bases = torch.randint(0, 4, (n_seq, L),
+                                      generator=torch.Generator().manual_seed(100))
+            lo, hi = shard_range(n_seq, rank, world)
+            h_bases = all_bases[lo:hi].to(torch.int8).pin_memory()
+            warm = h_bases[:1].to(dev)
+            cb.saturation_mutagenesis(model, warm, 1000, 1010)         # warm-up
+            h_d = h_j = None
+            if rank == 0:
+                h_d = torch.empty((n_seq, model.n_groups, 4, L), dtype=torch.float32,
+                                  pin_memory=True)
+                h_j = torch.empty((n_seq, 4, L), dtype=torch.float32, pin_memory=True)
             torch.cuda.synchronize()
             barrier(world)
             i_s = torch.cuda.Event(enable_timing=True)
             i_e = torch.cuda.Event(enable_timing=True)
             i_s.record()
-            d, j = cb.saturation_mutagenesis(model, bases, 0, L, mutant_batch=args.batch)
+            d_bases = h_bases.to(dev, non_blocking=True)
+            d, j = cb.saturation_mutagenesis(model, d_bases, 0, L, mutant_batch=args.batch)
+            if world > 1:
+                d, j = gather_shards(d, n_seq), gather_shards(j, n_seq)
+            if rank == 0:
+                h_d.copy_(d, non_blocking=True)
+                h_j.copy_(j, non_blocking=True)
             i_e.record()
             torch.cuda.synchronize()
             barrier(world)
             ism_ms = max_over_ranks(i_s.elapsed_time(i_e), world, dev)
-            n_mut = world * args.ism_seqs * 3 * L
+            n_mut = n_seq * 3 * L
             ism = {"value": n_mut / (ism_ms / 1000.0), "unit": "mutants/s",
-                   "mutants": n_mut, "ms": ism_ms,
-                   "workload": "{} random 2114-bp sequences per GPU x all 3x2114 single-base "
-                               "substitutions, delta log-count + profile JSD per mutant, "
-                               "{} mode".format(args.ism_seqs, args.mode)}
+                   "mutants": n_mut, "ms": ism_ms, "n_gpus": world,
+                   "scaling": "strong",
+                   "h2d_bytes": n_seq * L, "d2h_bytes": 4 * n_seq * L * (model.n_groups + 1) * 4,
+                   "workload": "{} random 2114-bp sequences (global, split over {} GPU(s)) x all "
+                               "3x2114 single-base substitutions, delta log-count + profile JSD "
+                               "per mutant, {} mode; H2D of bases, all-gather and D2H of the "
+                               "scores inside the timed region".format(n_seq, world, args.mode)}
 
     peaks, peak_src = load_peaks()
     mlp_ms, mlp_n = per_class["mlp"]
     mlp_avg_ms = mlp_ms / max(mlp_n, 1)
-    # tensor work of the MLP launches of the timed steps over their device time
+    # tensor work of the MLP launches of the instrumented steps over their
+    # device time (events on the launching stream around every launch)
     mlp_flop_step = mlp_flop_per_seq(model) * forwards * args.batch
-    achieved = mlp_flop_step * args.steps / (mlp_ms / 1000.0) / 1e12
-    peak = peaks["bf16_tflops_sustained"]
+    achieved = mlp_flop_step * n_inst / (mlp_ms / 1000.0) / 1e12
+    # a millisecond-long step runs at the burst clock: the burst peak applies
+    peak = peaks["bf16_tflops"]
     model_tflops = value / world * forwards * flop_per_seq(model) / 1e12
     default_width = model.n_filters == 128 and model.expansion == 2
     C, H = model.n_filters, model.n_filters * model.expansion
@@ -461,27 +529,30 @@ def run_ours(args, world, rank, local):
                    else "mlp_wide_kernel" if C == 256 and args.mode == "bf16"
                    else "mlp_stream_kernel") + " (tcgen05 conv+LN+MLP+residual, one layer)",
         "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-        "peak_source": "{} bf16_tflops_sustained".format(peak_src),
-        "frac_of_burst": achieved / peaks["bf16_tflops"],
+        "peak_source": "{} bf16_tflops (burst)".format(peak_src),
+        "frac_of_sustained": achieved / peaks["bf16_tflops_sustained"],
         # DRAM bytes of one MLP launch of the default-width backbone: ncu
-        # dram__bytes_read.sum + write.sum of the layer-0 launch at batch 256
-        # (138.77 MB + 93.71 MB), scaled by the sequences processed
+        # dram__bytes_read.sum + write.sum of one launch at batch 256, scaled
+        # by the sequences processed (profiles/mlp_ws_kernel_bf16_b256.md)
         "traffic": (MLP_DRAM_BYTES_PER_SEQ * args.batch
                     if args.mode == "bf16" and default_width and not variant else None),
         "traffic_unit": "bytes per launch",
         "algorithmic_bytes": 2.0 * L * C * (2 if args.mode == "bf16" else 4) * args.batch,
         "flop_per_launch": 4.0 * C * H * L * args.batch, "avg_launch_ms": mlp_avg_ms,
-        "whole_forward_tflops_per_gpu": model_tflops,
-        "whole_forward_frac": model_tflops / peak,
-        "kernel_share": {k: v[0] / max(dev_ms, 1e-9) for k, v in per_class.items() if v[1]},
+        "whole_forward": {
+            "tflops_per_gpu": model_tflops, "flop_per_unit": forwards * flop_per_seq(model),
+            "frac": model_tflops / peak,
+            "frac_of_sustained": model_tflops / peaks["bf16_tflops_sustained"]},
+        "kernel_share": {k: v[0] / max(inst_ms, 1e-9) for k, v in per_class.items() if v[1]},
+        "instrumented_steps": n_inst,
     }
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         n_cpu = args.cpu_sample if not variant else max(1, args.cpu_sample // 8)
-        rate, cores, reps = cpu_forward_rate(args, n_cpu)
-        cpu = {"value": rate, "unit": unit, "cores": cores, "kind": "port",
-               "sample": "{} {}, fp32 eager no_grad, median of {} reps".format(
-                   n_cpu, unit.split("/")[0], reps)}
+        rate, cores, reps, kind = cpu_forward_rate(args, n_cpu)
+        cpu = {"value": rate, "unit": unit, "cores": cores, "kind": kind,
+               "sample": "{} {}, fp32 eager no_grad, median of {} reps, {}".format(
+                   n_cpu, unit.split("/")[0], reps, REF_WHAT[kind])}
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": unit, "n_gpus": world,
@@ -506,7 +577,8 @@ def main():
     ap.add_argument("--batch", type=int, default=None,
                     help="units per GPU per step (default: the workload's)")
     ap.add_argument("--mode", choices=["bf16", "fp32"], default="bf16")
-    ap.add_argument("--ism-seqs", type=int, default=4)
+    ap.add_argument("--ism-seqs", type=int, default=256,
+                    help="ISM sequences in total, split over the ranks (0: skip)")
     ap.add_argument("--cpu-sample", type=int, default=32)
     ap.add_argument("--ref-sample", type=int, default=16)
     ap.add_argument("--no-e2e", action="store_true")

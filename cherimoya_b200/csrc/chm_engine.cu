@@ -1166,6 +1166,12 @@ int32_t chm_read_status(void* workspace, chm_stream_t stream) {
   return s;
 }
 
+int32_t chm_noalloc_read_status(chm_stream_t stream) {
+  uint8_t* ws = nullptr;
+  CHM_TRY(noalloc_scratch(&ws));
+  return chm_read_status(ws, stream);
+}
+
 int64_t chm_last_launch_count(void) { return g_launches; }
 
 void chm_timing_enable(int32_t enable) { g_timing.enabled = (enable != 0); }

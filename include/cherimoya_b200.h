@@ -200,6 +200,14 @@ int32_t chm_forward_noalloc(const chm_model_desc* desc, const void* packed, int3
                             const void* x, int32_t input_dtype, const float* x_ctl,
                             float* profile, float* logcounts, chm_stream_t stream);
 
+/* The status word of chm_forward_noalloc: synchronises `stream`, then
+ * returns and clears the status that the kernels of the last
+ * chm_forward_noalloc calls on the current device recorded in the static
+ * scratch (CHM_ERR_DEVICE_TIMEOUT when a bounded device wait gave up, else
+ * CHM_OK). The counterpart of chm_read_status for callers that pass no
+ * workspace; it allocates nothing either. */
+int32_t chm_noalloc_read_status(chm_stream_t stream);
+
 /* Synchronises `stream`, returns and clears the device status word that
  * the kernels of the last calls recorded in `workspace`. */
 int32_t chm_read_status(void* workspace, chm_stream_t stream);

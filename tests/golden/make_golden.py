@@ -1,8 +1,10 @@
 """Generate golden input/output vectors from the upstream Cherimoya package.
 
-Run from the repository root on a machine with the upstream checkout:
+Run from the repository root on a machine with an upstream copy, named by
+$CHERIMOYA_REFERENCE (a checkout) or installed into baseline/_ref (see
+oracle/upstream.py):
 
-    python tests/golden/make_golden.py
+    CHERIMOYA_REFERENCE=<upstream checkout> python tests/golden/make_golden.py
 
 Each case is a ``.pt`` file holding the model config, its fp32 state_dict,
 the inputs and the outputs of the upstream CPU path (eager, ``no_grad``).
@@ -25,9 +27,9 @@ import sys
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-sys.path.insert(0, HERE)
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 
-from _refshim import import_reference  # noqa: E402
+from oracle.upstream import import_upstream  # noqa: E402
 
 
 def one_hot(idx):
@@ -130,7 +132,7 @@ def ism_case(ref, name, config, N, L, start, end, seed):
 
 
 def main():
-    ref = import_reference()
+    ref = import_upstream()
     torch.set_num_threads(8)
     cheri = ref.cheri
 
