@@ -56,7 +56,10 @@ def test_validate_and_sizes():
     ws2 = lib.chm_forward_workspace_bytes(ctypes.byref(d), 2)
     assert ws2 > ws1 > 2 * 2114 * 128 * 2
     d32 = _desc(mode=0)
-    assert lib.chm_forward_workspace_bytes(ctypes.byref(d32), 1) > ws1
+    # fp32 activations: twice the bytes per sequence (bf16 mode also holds the
+    # fixed-size partials of the fused statistics)
+    ws32 = [lib.chm_forward_workspace_bytes(ctypes.byref(d32), n) for n in (1, 2)]
+    assert ws32[1] - ws32[0] > ws2 - ws1
     assert lib.chm_ism_workspace_bytes(ctypes.byref(d), 4, 512) > 0
     assert lib.chm_variant_workspace_bytes(ctypes.byref(d), 10) > 0
     assert lib.chm_block_packed_bytes(128, 256) > 0
