@@ -152,7 +152,7 @@ bool per_example_pays(int batch, int L, int sms) {
 }
 
 struct FwdLayout {
-  size_t status, stats, stats2, xa, xb, total;
+  size_t status, stats, stats2, part, xa, xb, total;
 };
 
 FwdLayout fwd_layout(const Dims& m, int batch) {
@@ -161,6 +161,10 @@ FwdLayout fwd_layout(const Dims& m, int batch) {
   f.status = o; o = align_up(o + 256);
   f.stats = o; o = align_up(o + (size_t)batch * 8);
   f.stats2 = o; o = align_up(o + (size_t)batch * 8);
+  // unit partials of the fused statistics, one block of slots per CTA
+  f.part = o;
+  if (fused_stats_config(m))
+    o = align_up(o + (size_t)device_sms() * ws::kPartSlots * su::kUnits * sizeof(double2));
   const size_t act = (size_t)batch * m.L * m.CP * m.act_bytes();
   f.xa = o; o = align_up(o + act);
   f.xb = o; o = align_up(o + act);
@@ -411,10 +415,10 @@ int launch_stats(const Dims& m, const act_t* X, const float* convw, int dil, int
                  float2* stats, bool pdl, cudaStream_t st) {
   if constexpr (sizeof(act_t) == 2) {
     if (m.CP == 128) {
-      // the moment accumulation the MLP kernel's fused statistics use, so both
-      // give bit-identical statistics
+      // the unit decomposition the fused statistics of the MLP kernel use, so
+      // both give bit-identical statistics
       LaunchTimer timer(kKStats, st);
-      launch_k(pdl, stats_moments_kernel, dim3(batch), dim3(kMomThreads), 0, st,
+      launch_k(pdl, stats_units_kernel, dim3(batch), dim3(kStatsUnitThreads), 0, st,
                reinterpret_cast<const __nv_bfloat16*>(X), convw, dil, m.L, m.C, 1e-3f, stats);
       return launch_status();
     }
@@ -554,9 +558,8 @@ int run_forward_t(const Dims& m, const PackLayout& pl, const uint8_t* packed, in
     }
   }
   // block stack. With whole examples per CTA, the MLP launch of block i also
-  // computes block i+1's statistics from its output tiles where the history
-  // of the next dilation fits (ws::fused_stats_fit); the other blocks, the
-  // first included, get a standalone statistics pass.
+  // computes block i+1's statistics from its output, so only the first block
+  // has a standalone statistics pass.
   const int grid = std::min(n_tiles, device_sms());
   const bool per_example = fused_stats_config(m) && per_example_pays(batch, m.L, device_sms());
   bool have_stats = false;
@@ -569,11 +572,12 @@ int run_forward_t(const Dims& m, const PackLayout& pl, const uint8_t* packed, in
     MlpArgs a{};
     a.per_example = per_example ? 1 : 0;
     a.reverse = i & 1;
-    if (per_example && i + 1 < m.n_layers && ws::fused_stats_fit(dil, 1 << (i + 1))) {
+    if (per_example && i + 1 < m.n_layers) {
       const uint8_t* nlw = packed + pl.layers + pl.layer_stride * (i + 1);
       a.stats_next = stats_nxt;
       a.next_convw = reinterpret_cast<const float*>(nlw + pl.l_convw);
       a.next_dil = 1 << (i + 1);
+      a.stats_part = reinterpret_cast<double2*>(ws + f.part);
     }
     a.X_in = xa;
     a.X_out = xb;

@@ -20,7 +20,7 @@ constexpr int kHeadTaps = 75;   // fconv kernel size (upstream cherimoya.py:182-
 constexpr int kHeadPad = 37;
 constexpr int kTileRows = 128;  // MMA M
 
-enum : int { kStatusOk = 0, kStatusUnsupported = 2, kStatusTimeout = 5 };
+enum : int { kStatusOk = 0, kStatusTimeout = 5 };
 
 template <typename T> __device__ __forceinline__ float to_f32(T v);
 template <> __device__ __forceinline__ float to_f32<float>(float v) { return v; }
@@ -813,85 +813,123 @@ __global__ void __launch_bounds__(kStatsChainThreads, 2) stats_chain_kernel(
   }
 }
 
-// ---------------------------------------------------------------- statistics by moments
-// Per-example statistics of the next block's conv output
-//   y[l] = w0 x[l-d] + w1 x[l] + w2 x[l+d]   (x zero outside [0, L))
-// follow from per-channel moments of x alone:
-//   sum y   = sum_c (w0 + w1 + w2) S - w0 T - w2 H
-//   sum y^2 = sum_c (w0^2 + w1^2 + w2^2) Q - w0^2 QT - w2^2 QH
-//             + 2 (w0 w1 + w1 w2) P1 + 2 w0 w2 P2
-// with S, Q the sum and sum of squares of x over all rows, H, QH over rows
-// l < d, T, QT over rows l >= L - d, and the lag products
-// P1 = sum_l x[l] x[l-d], P2 = sum_l x[l] x[l-2d] (pairs inside [0, L)).
-// The MLP kernel accumulates them from each output tile while it is still in
-// shared memory; the standalone kernel reads x from global memory. Both use
-// one accumulation layout, so their statistics are bit-identical: thread
-// (p, h) of 128, p a channel pair (2p, 2p + 1), h a row half, adds in fp32
-// the rows l = 128 t + 64 h + j for tiles t = 0, 1, ... and j = 0 .. 63 in
-// that order; each thread's moments become fp64 sums (moments_finish), which
-// a warp reduces with a fixed xor tree and the four warps add in order.
-// bf16 activations, 128 channels (the default-width model).
-struct Moments {
-  f2 s, q, p1, p2, hs, hq, ts, tq;
+// ---------------------------------------------------------------- stats units
+// Per-example statistics of y = w0 x[l-d] + w1 x[l] + w2 x[l+d] for bf16
+// activations with 128 channels, split into a fixed set of work units so that
+// any number of threads, in any order, produces bit-identical results (the
+// standalone kernel below and the MLP kernel's fused next-layer statistics
+// share this decomposition):
+//   * chain segments as in stats_chain_kernel: row r = rho + k d lies on chain
+//     rho; segment (kb, rho) is chain positions kb*kS .. kb*kS + kS-1 (kS =
+//     12), read with one halo row on each side; segments are numbered
+//     s = kb d + rho (s = rho when d >= L), so a segment's rows grow with s;
+//   * unit (chunk c, lane q): 4 channels [4c, 4c + 4) (8 bytes per row) and the
+//     contiguous segment block [q n_seg / 16, (q + 1) n_seg / 16);
+//   * a segment's y and y^2 are summed in fp32 in a fixed order, a unit adds
+//     its segments' sums into fp64 in ascending s, and the 512 unit partials
+//     are combined in one fixed order (stats_combine).
+// A warp covers one lane q for all 32 chunks: every load is one whole 256-byte
+// row.
+namespace su {
+constexpr int kChunks = 32;                 // 4-channel chunks of a 128-channel row
+constexpr int kLanes = 16;                  // segment blocks per example
+constexpr int kUnits = kChunks * kLanes;    // 512
+constexpr int kS = 12;                      // chain positions per segment
+__host__ __device__ constexpr int n_kb(int L, int d) { return ((L + d - 1) / d + kS - 1) / kS; }
+__host__ __device__ constexpr int n_seg(int L, int d) { return d >= L ? L : d * n_kb(L, d); }
+__host__ __device__ constexpr int seg_lo(int q, int ns) { return (int)((long long)q * ns / kLanes); }
+// first row of segment s (its centre row at chain position kb * kS)
+__host__ __device__ constexpr int seg_r0(int s, int L, int d) {
+  return d >= L ? s : (s % d) + (s / d) * kS * d;
+}
+// rows [0, need) must be final before lane q's segments can be read
+__host__ __device__ inline int lane_rows_needed(int q, int L, int d) {
+  const int ns = n_seg(L, d);
+  const int s1 = seg_lo(q + 1, ns);
+  if (s1 <= seg_lo(q, ns)) return 0;
+  const long long last = (long long)seg_r0(s1 - 1, L, d) + (long long)kS * d;  // right halo
+  return last >= L ? L : static_cast<int>(last) + 1;
+}
+}  // namespace su
+
+// fp32 conv weights of chunk c: pairs (4c, 4c+1), (4c+2, 4c+3) per tap
+struct StatsW {
+  f2 w0[2], w1[2], w2[2];
 };
-__device__ __forceinline__ void moments_zero(Moments& m) {
-  m.s = m.q = m.p1 = m.p2 = m.hs = m.hq = m.ts = m.tq = f2{0.f, 0.f};
-}
-__device__ __forceinline__ f2 bf2_unpack(uint32_t w) {
-  return f2{__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u)};
-}
-// x: row l's channel pair; xa, xb: rows l - d and l - 2d (0 outside [0, L))
-__device__ __forceinline__ void moments_add(Moments& m, uint32_t x, uint32_t xa, uint32_t xb,
-                                            int l, int L, int d) {
-  const f2 v = bf2_unpack(x);
-  m.s = f2{m.s.x + v.x, m.s.y + v.y};
-  m.q = fma2(v, v, m.q);
-  m.p1 = fma2(v, bf2_unpack(xa), m.p1);
-  m.p2 = fma2(v, bf2_unpack(xb), m.p2);
-  if (l < d) {
-    m.hs = f2{m.hs.x + v.x, m.hs.y + v.y};
-    m.hq = fma2(v, v, m.hq);
-  }
-  if (l >= L - d) {
-    m.ts = f2{m.ts.x + v.x, m.ts.y + v.y};
-    m.tq = fma2(v, v, m.tq);
-  }
-}
-// (sum y, sum y^2) of this thread's two channels, fp64; convw = the next
-// block's (3, 128) fp32 conv weights
-__device__ __forceinline__ double2 moments_finish(const Moments& m,
-                                                  const float* __restrict__ convw, int p, int C) {
+__device__ __forceinline__ StatsW stats_weights(const float* __restrict__ convw, int c, int C) {
   constexpr int CP = 128;
-  double sy = 0.0, sq = 0.0;
+  StatsW w;
 #pragma unroll
-  for (int e = 0; e < 2; ++e) {
-    const int c = 2 * p + e;
-    const double w0 = c < C ? convw[c] : 0.0;
-    const double w1 = c < C ? convw[CP + c] : 0.0;
-    const double w2 = c < C ? convw[2 * CP + c] : 0.0;
-    const double S = e ? m.s.y : m.s.x, Q = e ? m.q.y : m.q.x;
-    const double P1 = e ? m.p1.y : m.p1.x, P2 = e ? m.p2.y : m.p2.x;
-    const double H = e ? m.hs.y : m.hs.x, QH = e ? m.hq.y : m.hq.x;
-    const double T = e ? m.ts.y : m.ts.x, QT = e ? m.tq.y : m.tq.x;
-    sy += (w0 + w1 + w2) * S - w0 * T - w2 * H;
-    sq += (w0 * w0 + w1 * w1 + w2 * w2) * Q - w0 * w0 * QT - w2 * w2 * QH +
-          2.0 * (w0 * w1 + w1 * w2) * P1 + 2.0 * w0 * w2 * P2;
+  for (int m = 0; m < 2; ++m) {
+    const int ch = 4 * c + 2 * m;
+    w.w0[m] = f2{ch < C ? convw[ch] : 0.f, ch + 1 < C ? convw[ch + 1] : 0.f};
+    w.w1[m] = f2{ch < C ? convw[CP + ch] : 0.f, ch + 1 < C ? convw[CP + ch + 1] : 0.f};
+    w.w2[m] = f2{ch < C ? convw[2 * CP + ch] : 0.f, ch + 1 < C ? convw[2 * CP + ch + 1] : 0.f};
   }
-  return make_double2(sy, sq);
+  return w;
 }
-// xor-tree reduction of a warp; lane 0's value is the one used
-__device__ __forceinline__ double2 warp_sum_d2(double2 v) {
+
+// Unit (c, q) of one example: Xe points at the example's first row as 8-byte
+// chunks (32 per row). Loads go through L2 only (the rows may have been
+// written by this kernel's bulk stores).
+__device__ __forceinline__ double2 stats_unit(const uint2* __restrict__ Xe, int c, int q,
+                                              const StatsW& w, int d, int L) {
+  using namespace su;
+  const int ns = n_seg(L, d);
+  const int s1 = seg_lo(q + 1, ns);
+  double S = 0.0, Q = 0.0;
+  for (int s = seg_lo(q, ns); s < s1; ++s) {
+    const int r0 = seg_r0(s, L, d);
+    if (r0 >= L) continue;
+    uint2 v[kS + 2];                                   // rows r0 + (j - 1) d
+#pragma unroll
+    for (int j = 0; j < kS + 2; ++j) {
+      const long long r = (long long)r0 + (long long)(j - 1) * d;
+      v[j] = (r >= 0 && r < L) ? ld_cg_u2(Xe + r * kChunks + c) : make_uint2(0u, 0u);
+    }
+    f2 sy0{0.f, 0.f}, sy1{0.f, 0.f}, sq0{0.f, 0.f}, sq1{0.f, 0.f};
+#pragma unroll
+    for (int j = 1; j <= kS; ++j) {
+      if ((long long)r0 + (long long)(j - 1) * d < L) {
+        const f2 l0{__uint_as_float(v[j - 1].x << 16), __uint_as_float(v[j - 1].x & 0xFFFF0000u)};
+        const f2 l1{__uint_as_float(v[j - 1].y << 16), __uint_as_float(v[j - 1].y & 0xFFFF0000u)};
+        const f2 c0{__uint_as_float(v[j].x << 16), __uint_as_float(v[j].x & 0xFFFF0000u)};
+        const f2 c1{__uint_as_float(v[j].y << 16), __uint_as_float(v[j].y & 0xFFFF0000u)};
+        const f2 r0v{__uint_as_float(v[j + 1].x << 16), __uint_as_float(v[j + 1].x & 0xFFFF0000u)};
+        const f2 r1v{__uint_as_float(v[j + 1].y << 16), __uint_as_float(v[j + 1].y & 0xFFFF0000u)};
+        const f2 y0 = fma2(w.w0[0], l0, fma2(w.w1[0], c0, mul2(w.w2[0], r0v)));
+        const f2 y1 = fma2(w.w0[1], l1, fma2(w.w1[1], c1, mul2(w.w2[1], r1v)));
+        sy0 = f2{sy0.x + y0.x, sy0.y + y0.y};
+        sy1 = f2{sy1.x + y1.x, sy1.y + y1.y};
+        sq0 = fma2(y0, y0, sq0);
+        sq1 = fma2(y1, y1, sq1);
+      }
+    }
+    S += static_cast<double>((sy0.x + sy0.y) + (sy1.x + sy1.y));
+    Q += static_cast<double>((sq0.x + sq0.y) + (sq1.x + sq1.y));
+  }
+  return make_double2(S, Q);
+}
+
+// The fixed-order combine of an example's 512 unit partials (part[q * 32 + c])
+// by one warp; lane 0's result is the statistics (mean, rstd). kGlobal: the
+// partials are in global memory (read through L2), else in shared memory.
+template <bool kGlobal>
+__device__ __forceinline__ float2 stats_combine(const double2* part, int lane, int L, int C,
+                                                float eps) {
+  double S = 0.0, Q = 0.0;
+#pragma unroll 4
+  for (int q = 0; q < su::kLanes; ++q) {
+    const double2 p = kGlobal ? ld_cg_d2(part + q * su::kChunks + lane)
+                              : part[q * su::kChunks + lane];
+    S += p.x;
+    Q += p.y;
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
-    v.x += __shfl_xor_sync(0xffffffffu, v.x, o);
-    v.y += __shfl_xor_sync(0xffffffffu, v.y, o);
+    S += __shfl_xor_sync(0xffffffffu, S, o);
+    Q += __shfl_xor_sync(0xffffffffu, Q, o);
   }
-  return v;
-}
-// the four warp sums, added in warp order -> (mean, rstd)
-__device__ __forceinline__ float2 moments_stats(const double2* w, int L, int C, float eps) {
-  const double S = ((w[0].x + w[1].x) + w[2].x) + w[3].x;
-  const double Q = ((w[0].y + w[1].y) + w[2].y) + w[3].y;
   const double n = static_cast<double>(L) * static_cast<double>(C);
   const double mean = S / n;
   double var = Q / n - mean * mean;
@@ -901,36 +939,23 @@ __device__ __forceinline__ float2 moments_stats(const double2* w, int L, int C, 
 }
 
 // Standalone statistics of bf16 activations with 128 channels (the first
-// block's input, the blocks whose statistics the MLP kernel does not fuse,
-// small batches): one 128-thread block per example.
-constexpr int kMomThreads = 128;
-__global__ void __launch_bounds__(kMomThreads) stats_moments_kernel(
+// block's input, and any launch without fused statistics): one block per
+// example, warp q = segment block, lane = chunk, one unit per thread.
+constexpr int kStatsUnitThreads = su::kLanes * 32;   // 512
+__global__ void __launch_bounds__(kStatsUnitThreads, 1) stats_units_kernel(
     const __nv_bfloat16* __restrict__ X, const float* __restrict__ convw, int dil, int L, int C,
     float eps, float2* __restrict__ stats) {
-  __shared__ double2 red[4];
-  const int b = blockIdx.x, tid = threadIdx.x, p = tid & 63, h = tid >> 6;
+  __shared__ double2 part[su::kUnits];
+  const int b = blockIdx.x, lane = threadIdx.x & 31, q = threadIdx.x >> 5;
+  const StatsW w = stats_weights(convw, lane, C);
   griddep_wait();                          // the previous kernel's outputs are visible
-  const uint32_t* Xe = reinterpret_cast<const uint32_t*>(X + (size_t)b * L * 128) + p;
-  Moments m;
-  moments_zero(m);
-  const int tpe = (L + kTileRows - 1) / kTileRows;
-  for (int t = 0; t < tpe; ++t) {
-    const int r0 = t * kTileRows + h * 64;
-#pragma unroll 8
-    for (int j = 0; j < 64; ++j) {
-      const int l = r0 + j;
-      if (l < L) {
-        const uint32_t x = __ldg(Xe + (size_t)l * 64);
-        const uint32_t xa = l - dil >= 0 ? __ldg(Xe + (size_t)(l - dil) * 64) : 0u;
-        const uint32_t xb = l - 2 * dil >= 0 ? __ldg(Xe + (size_t)(l - 2 * dil) * 64) : 0u;
-        moments_add(m, x, xa, xb, l, L, dil);
-      }
-    }
-  }
-  const double2 v = warp_sum_d2(moments_finish(m, convw, p, C));
-  if ((tid & 31) == 0) red[tid >> 5] = v;
+  const uint2* Xe = reinterpret_cast<const uint2*>(X + (size_t)b * L * 128);
+  part[q * su::kChunks + lane] = stats_unit(Xe, lane, q, w, dil, L);
   __syncthreads();
-  if (tid == 0) stats[b] = moments_stats(red, L, C, eps);
+  if (q == 0) {
+    const float2 r = stats_combine<false>(part, lane, L, C, eps);
+    if (lane == 0) stats[b] = r;
+  }
 }
 
 // ============================================================== MLP
@@ -966,6 +991,7 @@ struct MlpArgs {
   float2* stats_next;    // statistics of the next block (nullptr: not computed here)
   const float* next_convw;   // (3, CP) fp32 conv weights of the next block
   int next_dil;
+  double2* stats_part;   // unit partials: gridDim.x * ws::kPartSlots * su::kUnits
 };
 
 template <int CP, int HP>
@@ -1748,7 +1774,10 @@ constexpr int kProducerWarps = 4, kEpilogueWarps = 8, kResidualWarps = 4;
 constexpr int kResidualWarp0 = kProducerWarps + kEpilogueWarps; // 12
 constexpr int kMmaWarp = kResidualWarp0 + kResidualWarps;       // 16
 constexpr int kTmaWarp = kMmaWarp + 1;                          // 17
-constexpr int kThreads = (kTmaWarp + 1) * 32;                   // 576
+constexpr int kStatsWarp0 = kTmaWarp + 1;                       // 18
+constexpr int kStatsWarps = 2;
+constexpr int kThreads = (kStatsWarp0 + kStatsWarps) * 32;      // 640 (96 registers)
+constexpr int kPartSlots = 4;           // examples whose unit partials are in flight per CTA
 constexpr uint32_t kResBox = 128 * 128;                         // 16 KB residual box
 constexpr uint32_t kW1 = 0;                                     // 256 x 128 bf16
 constexpr uint32_t kW2 = kW1 + kH * kC * 2;                     // 128 x 256 bf16
@@ -1756,7 +1785,7 @@ constexpr uint32_t kStg = kW2 + kC * kH * 2;                    // staging ring
 constexpr int kMaxSlots = 5;
 enum Bar : int { STG_FULL0 = 0, STG_EMPTY0 = kMaxSlots, A1_FULL0 = 2 * kMaxSlots, A1_FULL1,
                  A1_EMPTY0, A1_EMPTY1, D1A_FULL, D1B_FULL, A2A_FULL, A2B_FULL, D2_FULL,
-                 RES_FULL, RES_DONE, D2_EMPTY, MOM_READ, MOM_HIST, MOM_RED, kNumBars };
+                 RES_FULL, RES_DONE, D2_EMPTY, kNumBars };
 // Staging ring. Split mode (any dilation): a box step covers kBoxBytes of
 // channels and a slot holds its three 128-row blocks (rows - d, rows,
 // rows + d), 64-byte rows with the 64-byte swizzle. Wide mode (bf16, d <= 64):
@@ -1775,9 +1804,10 @@ struct Layout {
   static constexpr uint32_t kBars = kConvW + 3 * kC * 4;
   static constexpr uint32_t kSlot = kBars + kNumBars * 8;
   static constexpr uint32_t kAbort = kSlot + 4;
-  // fused statistics: the four residual warps' fp64 sums
-  static constexpr uint32_t kRed = (kAbort + 4 + 15) & ~15u;
-  static constexpr uint32_t kAlloc = kRed + 4 * 16 + 1024;
+  // fused statistics: tiles stored, work-item counter, per-slot done counts
+  // and generations
+  static constexpr uint32_t kCtl = kAbort + 4;
+  static constexpr uint32_t kAlloc = kCtl + (2 + 2 * kPartSlots) * 4 + 1024;
   static_assert(kSlots <= kMaxSlots, "staging ring depth");
   static_assert(kAlloc <= 232448, "shared memory per block");
   static_assert(!kWide || sizeof(act_t) == 2, "wide staging is for bf16 activations");
@@ -1790,18 +1820,6 @@ constexpr int kWideMaxDil = 64;
 // rows of a wide staging block: 128 + 2d rounded up to whole 8-row swizzle
 // atoms (at most 256, the TMA box limit)
 __host__ __device__ constexpr int wide_rows(int dil) { return (kTileRows + 2 * dil + 7) & ~7; }
-// Wide staging slots hold wide_rows(d) 128-byte rows (1 KB aligned for the
-// swizzle); the rest of the 64 KB staging region holds the fused statistics'
-// history: the last 2 d' rows (256 bytes each) of the previous output tile,
-// d' the next block's dilation. Fusion needs 2 d' <= 128 (history within one
-// tile) and room for the history.
-__host__ __device__ constexpr uint32_t wide_slot_bytes(int dil) {
-  return (static_cast<uint32_t>(wide_rows(dil)) * 128u + 1023u) & ~1023u;
-}
-__host__ __device__ constexpr bool fused_stats_fit(int dil, int next_dil) {
-  return dil <= kWideMaxDil && next_dil >= 1 && 2 * next_dil <= kTileRows &&
-         static_cast<uint32_t>(2 * next_dil) * 256u + 2u * wide_slot_bytes(dil) <= 2u * 256u * 128u;
-}
 constexpr uint32_t kD2Col = 256, kA1Col = 384;
 // TMEM column of the packed bf16 A2 for K-step s (16 h values) of a half
 __host__ __device__ constexpr uint32_t a2_col(int s) { return s < 4 ? 8 * s : 64 + 8 * (s - 4); }
@@ -1820,7 +1838,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
   using Lay = Layout<act_t, kWide>;
   constexpr uint32_t kBoxBytes = Lay::kBoxBytes, kBox = Lay::kBox, kSlotBytes = Lay::kSlotBytes;
   constexpr uint32_t kRes = Lay::kRes, kConvW = Lay::kConvW, kBars = Lay::kBars;
-  constexpr uint32_t kSlot = Lay::kSlot, kAbort = Lay::kAbort, kRed = Lay::kRed;
+  constexpr uint32_t kSlot = Lay::kSlot, kAbort = Lay::kAbort, kCtl = Lay::kCtl;
   constexpr int kSlots = Lay::kSlots;
   constexpr int kCPR = kBoxBytes / 16;                 // 16-byte chunks per staging row
   extern __shared__ uint8_t smem_raw[];
@@ -1829,18 +1847,20 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBars);
   uint32_t* slot = reinterpret_cast<uint32_t*>(smem + kSlot);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kAbort);
+  // fused statistics control words: tiles of this CTA whose stores have
+  // completed, next work item, per partial slot the finished-item count and
+  // the example that may use it next
+  int* ctl = reinterpret_cast<int*>(smem + kCtl);
+  volatile int* tiles_stored = ctl;
+  int* item_next = ctl + 1;
+  int* slot_done = ctl + 2;
+  volatile int* slot_gen = ctl + 2 + kPartSlots;
   const float* sConvW = reinterpret_cast<const float*>(smem + kConvW);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  constexpr bool kTmaResidual = sizeof(act_t) == 2;
-  // staging slot stride (wide: just the rows a step needs) and the fused
-  // statistics' history buffer behind the slots
-  const uint32_t slot_stride = kWide ? wide_slot_bytes(a.dil) : kSlotBytes;
-  const uint32_t kHist = kStg + kSlots * slot_stride;
-  const bool fuse = kWide && kTmaResidual && a.stats_next != nullptr && a.per_example &&
-                    fused_stats_fit(a.dil, a.next_dil);
-  if (tid == 0 && a.stats_next != nullptr && !fuse) atomicExch(a.status, kStatusUnsupported);
+  const bool fuse = (sizeof(act_t) == 2) && a.stats_next != nullptr && a.per_example;
   const act_t* Xi = static_cast<const act_t*>(a.X_in);
   act_t* Xo = static_cast<act_t*>(a.X_out);
+  constexpr bool kTmaResidual = sizeof(act_t) == 2;
   constexpr int kBoxCh = kBoxBytes / sizeof(act_t);             // channels per box step
   constexpr int kBoxes = kC / kBoxCh;                           // box steps per tile
 
@@ -1853,11 +1873,17 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
         count = kProducerWarps;
       else if (i == A2A_FULL || i == A2B_FULL)
         count = kEpilogueWarps;
-      else if (i == RES_DONE || i == D2_EMPTY || i == MOM_READ || i == MOM_HIST || i == MOM_RED)
+      else if (i == RES_DONE || i == D2_EMPTY)
         count = kResidualWarps;
       mbar_init(&bars[i], count);
     }
     *abort_flag = 0;
+    ctl[0] = 0;
+    ctl[1] = 0;
+    for (int i = 0; i < kPartSlots; ++i) {
+      ctl[2 + i] = 0;
+      ctl[2 + kPartSlots + i] = i;
+    }
     mbar_init_fence();
   }
   {
@@ -1914,55 +1940,64 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
     return a.n_tiles - 1 - (first + tit * stride);
   };
 
-  // Statistics of the next block (fused, whole examples per CTA): after each
-  // output tile is complete in the residual buffer, the residual warps add its
-  // rows to the moments of the next block's conv (statistics by moments,
-  // above), thread (p, h) = (channel pair, row half). Rows l - d' and l - 2d'
-  // before the tile come from the history buffer, which then takes this
-  // tile's last 2 d' rows. After an example's last tile the four warps' sums
-  // give its statistics.
-  Moments mom;
-  moments_zero(mom);
-  auto moments_tile = [&](int it) -> bool {
-    const int k = it / tpe, t = it - k * tpe;
-    const int rl = (warp & 3) * 32 + lane;
-    const int p = rl & 63, h = rl >> 6;
-    const int L = a.L, nd = a.next_dil;
-    const int l0 = t * kTileRows;
-    const uint8_t* box = smem + kRes + (p >> 5) * kResBox;
-    const uint32_t cb = static_cast<uint32_t>(p & 31) * 4u;   // byte of the pair in its 128-byte row
-    auto rd = [&](int r) -> uint32_t {                         // pair p of tile row r (swizzled box)
-      return *reinterpret_cast<const uint32_t*>(
-          box + r * 128 + ((((cb >> 4) ^ static_cast<uint32_t>(r & 7)) << 4) | (cb & 15u)));
-    };
-    uint32_t* hist = reinterpret_cast<uint32_t*>(smem + kHist);   // row i: pairs hist[64 i ..]
-    if (!mbar_wait_abortable(&bars[RES_DONE], it & 1, abort_flag)) return false;
-    for (int j = 0; j < 64; ++j) {
-      const int r = h * 64 + j, l = l0 + r;
-      if (l >= L) break;
-      const int ra = r - nd, rb = r - 2 * nd;
-      const uint32_t x = rd(r);
-      const uint32_t xa = ra >= 0 ? rd(ra) : (l - nd >= 0 ? hist[(ra + 2 * nd) * 64 + p] : 0u);
-      const uint32_t xb = rb >= 0 ? rd(rb) : (l - 2 * nd >= 0 ? hist[(rb + 2 * nd) * 64 + p] : 0u);
-      moments_add(mom, x, xa, xb, l, L, nd);
+  // Statistics of the next block (fused): work item = (example k of this CTA,
+  // segment block q) covering units (c = lane, q) of su::; claimed in order by
+  // whichever warp is free (the statistics warps from the start, the pipeline
+  // warps once their last tile is done). An item waits until the rows it reads
+  // are stored; the warp finishing an example's last item combines its 512
+  // partials in the fixed order. Partials of up to kPartSlots examples are in
+  // flight per CTA (global scratch, L2).
+  auto stats_work = [&]() {
+    if constexpr (sizeof(act_t) == 2) {
+      const StatsW w = stats_weights(a.next_convw, lane, a.C);
+      const int L = a.L, d = a.next_dil;
+      const int n_items = n_ex * su::kLanes;
+      double2* part_cta = a.stats_part + (size_t)blockIdx.x * kPartSlots * su::kUnits;
+      const uint2* Xo2 = reinterpret_cast<const uint2*>(a.X_out);
+      for (;;) {
+        int item = 0;
+        if (lane == 0) item = atomicAdd(item_next, 1);
+        item = __shfl_sync(0xffffffffu, item, 0);
+        if (item >= n_items) break;
+        const int k = item / su::kLanes, q = item - k * su::kLanes;
+        const int ps = k % kPartSlots;
+        const int need = su::lane_rows_needed(q, L, d);
+        bool ok = true;
+        const uint64_t t0 = global_ns();
+        for (uint32_t spin = 0;; ++spin) {
+          const int done_tiles = min(max(*tiles_stored - k * tpe, 0), tpe);
+          if (min(done_tiles * kTileRows, L) >= need && slot_gen[ps] == k) break;
+          if ((spin & 15u) == 15u && (*abort_flag || global_ns() - t0 > kWaitNs)) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          __nanosleep(128);
+        }
+        if (!ok) break;
+        __threadfence();          // the rows' stores (published before tiles_stored) first
+        const uint2* Xe = Xo2 + (size_t)ex_of(k) * L * su::kChunks;
+        double2* part = part_cta + ps * su::kUnits;
+        st_cg_d2(part + q * su::kChunks + lane, stats_unit(Xe, lane, q, w, d, L));
+        __threadfence_block();
+        __syncwarp();
+        int prev = 0;
+        if (lane == 0) prev = atomicAdd(&slot_done[ps], 1);
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        if (prev == su::kLanes - 1) {
+          // last item of example k: every partial is written
+          __threadfence_block();
+          const float2 st = stats_combine<true>(part, lane, L, a.C, 1e-3f);
+          if (lane == 0) {
+            a.stats_next[ex_of(k)] = st;
+            slot_done[ps] = 0;
+            __threadfence_block();
+            slot_gen[ps] = k + kPartSlots;
+          }
+          __syncwarp();
+        }
+      }
     }
-    mbar_arrive_warp(&bars[MOM_READ]);
-    if (!mbar_wait_abortable(&bars[MOM_READ], it & 1, abort_flag)) return false;
-    if (t + 1 < tpe) {
-      for (int i = h; i < 2 * nd; i += 2) hist[i * 64 + p] = rd(kTileRows - 2 * nd + i);
-    }
-    mbar_arrive_warp(&bars[MOM_HIST]);
-    if (!mbar_wait_abortable(&bars[MOM_HIST], it & 1, abort_flag)) return false;
-    if (t + 1 == tpe) {
-      double2* red = reinterpret_cast<double2*>(smem + kRed);
-      const double2 v = warp_sum_d2(moments_finish(mom, a.next_convw, p, a.C));
-      if (lane == 0) red[warp & 3] = v;
-      mbar_arrive_warp(&bars[MOM_RED]);
-      if (!mbar_wait_abortable(&bars[MOM_RED], k & 1, abort_flag)) return false;
-      if (rl == 0) a.stats_next[ex_of(k)] = moments_stats(red, L, a.C, 1e-3f);
-      moments_zero(mom);
-    }
-    return true;
   };
 
   if (warp < kProducerWarps) {
@@ -2002,7 +2037,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
         if constexpr (kWide) {
           // rows rl, rl + d, rl + 2d of the slot's block are this thread's
           // x[l - d], x[l], x[l + d]; two passes of 32 channels
-          const uint8_t* blk = smem + kStg + slotk * slot_stride;
+          const uint8_t* blk = smem + kStg + slotk * kSlotBytes;
           const uint32_t* cw2 = reinterpret_cast<const uint32_t*>(smem + kConvW);
           const int rm = rl, rc = rl + a.dil, rp = rl + 2 * a.dil;
 #pragma unroll
@@ -2248,16 +2283,23 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
           tma_store_3d(&maps.out, sRes, 0, l0, n);        // rows past L are clipped
           tma_store_3d(&maps.out, sRes + kResBox, 64, l0, n);
           bulk_commit();
-        }
-        // fused statistics: the output tile's moments (all four warps), read
-        // before the buffer takes the next tile's input
-        if (fuse && !moments_tile(it)) break;
-        if (leader) {
+          // fused statistics read the stored rows: publish how many tiles'
+          // stores have completed (all but the one just issued, or all)
+          auto publish = [&](int tiles) {
+            fence_proxy_async_global();
+            __threadfence();
+            *tiles_stored = tiles;
+          };
           if (it + 1 < n_my) {
             bulk_wait_read0();                            // the tile buffer is free again
             load_res(it + 1);
+            if (fuse) {
+              bulk_wait1();
+              publish(it);
+            }
           } else {
             bulk_wait0();                                 // stores complete before exit
+            if (fuse) publish(n_my);
           }
         }
       } else {
@@ -2388,7 +2430,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
         if constexpr (kWide) {
           // one block of rows [l0 - d, l0 - d + wide_rows(d)) (the map's box)
           mbar_expect_tx(&bars[STG_FULL0 + slotk], wide_rows(a.dil) * kBoxBytes);
-          tma_load_3d(smem + kStg + slotk * slot_stride, &maps.stage, b * kBoxCh, l0 - a.dil, n,
+          tma_load_3d(smem + kStg + slotk * kSlotBytes, &maps.stage, b * kBoxCh, l0 - a.dil, n,
                       &bars[STG_FULL0 + slotk]);
         } else {
           mbar_expect_tx(&bars[STG_FULL0 + slotk], kSlotBytes);
@@ -2423,7 +2465,13 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       }
     }
     __syncwarp();
+  } else {
+    // ------------------------------------------------------------ statistics warps
+    if (fuse) stats_work();
   }
+  // the producer, GELU and residual warps take the statistics items left once
+  // their last tile is done
+  if (fuse && warp < kMmaWarp && !*abort_flag) stats_work();
   // drain: every MMA this CTA issued has been waited on by the residual
   // warps (D2_FULL of the last tile) unless the pipeline aborted.
   tc_fence_before();

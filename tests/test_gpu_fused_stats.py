@@ -1,16 +1,15 @@
 """The MLP kernel's fused next-block LayerNorm statistics.
 
 In bf16 mode at the default width, a batch large enough for whole examples
-per CTA (at least one example per SM, e.g. 296 = 2 x 148 sequences) has
-each MLP launch of blocks 0-4 accumulate, from every output tile while it is
-still in shared memory, the per-channel moments from which the next block's
-statistics follow (sums, squares and lag-d / lag-2d products); a small batch
-computes the same moments in a standalone pass over global memory. Both use
-one accumulation order and one combine order, and the per-tile MLP
-arithmetic does not depend on which CTA runs a tile, so a sequence's outputs
-must be bitwise equal on both paths. The large batch is also checked against
-the oracle on sampled rows (bf16 tolerances: max abs error <= 1e-2,
-per-track profile Pearson >= 0.9999).
+per CTA (at least one example per SM, e.g. 296 = 2 x 148 sequences) runs
+every block's MLP launch with the next block's statistics computed inside it
+from the rows it has just stored; a small batch computes them in a standalone
+pass. Both use the same fixed decomposition of the statistics into work
+units and the same combine order, and the per-tile MLP arithmetic does not
+depend on which CTA runs a tile, so a sequence's outputs must be bitwise
+equal on both paths. The large batch is also checked against the oracle on
+sampled rows (bf16 tolerances: max abs error <= 1e-2, per-track profile
+Pearson >= 0.9999).
 """
 
 import pytest
