@@ -128,31 +128,8 @@ PackLayout pack_layout(const Dims& m) {
 }
 
 // ---- forward workspace layout (for `batch` rows)
-int device_sms() {
-  int dev = 0, sms = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
-  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
-  return sms > 0 ? sms : 148;
-}
-
-// the warp-specialised MLP kernel (and with it the fused next-block
-// statistics) runs for bf16 activations at n_filters <= 128, hidden 256
-bool fused_stats_config(const Dims& m) {
-  return m.mode == CHM_MODE_BF16 && m.CP == ws::kC && m.HP == ws::kH;
-}
-
-// Whole examples per CTA pay when the per-example makespan (ceil(batch / SMs)
-// examples of tpe tiles) stays within 1.3x of dealing single tiles, the
-// standalone statistics pass it removes costing about that much.
-bool per_example_pays(int batch, int L, int sms) {
-  const long long tpe = (L + kTileRows - 1) / kTileRows;
-  const long long ex_tiles = (long long)((batch + sms - 1) / sms) * tpe;
-  const long long tile_tiles = ((long long)batch * tpe + sms - 1) / sms;
-  return batch >= sms && ex_tiles * 10 <= tile_tiles * 13;
-}
-
 struct FwdLayout {
-  size_t status, stats, stats2, part, xa, xb, total;
+  size_t status, stats, xa, xb, total;
 };
 
 FwdLayout fwd_layout(const Dims& m, int batch) {
@@ -160,16 +137,18 @@ FwdLayout fwd_layout(const Dims& m, int batch) {
   size_t o = 0;
   f.status = o; o = align_up(o + 256);
   f.stats = o; o = align_up(o + (size_t)batch * 8);
-  f.stats2 = o; o = align_up(o + (size_t)batch * 8);
-  // unit partials of the fused statistics, one block of slots per CTA
-  f.part = o;
-  if (fused_stats_config(m))
-    o = align_up(o + (size_t)device_sms() * ws::kPartSlots * su::kUnits * sizeof(double2));
   const size_t act = (size_t)batch * m.L * m.CP * m.act_bytes();
   f.xa = o; o = align_up(o + act);
   f.xb = o; o = align_up(o + act);
   f.total = o;
   return f;
+}
+
+int device_sms() {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
+  return sms > 0 ? sms : 148;
 }
 
 // Launch `k`; with `pdl` under programmatic stream serialization, so the grid
@@ -309,8 +288,7 @@ int launch_mlp(const Dims& m, const MlpArgs& a, int grid, cudaStream_t st) {
     MlpArgs ae = a;
     ae.tpe = (m.L + kTileRows - 1) / kTileRows;
     ae.n_tiles = batch * ae.tpe;
-    ae.batch = batch;
-    const int egrid = std::max(1, std::min(ae.per_example ? batch : ae.n_tiles, device_sms()));
+    const int egrid = std::max(1, std::min(ae.n_tiles, device_sms()));
     MlpMaps tmap;
     // bf16 residual: the input tile is read and the output tile written by TMA
     CHM_TRY(make_act_tmap3_box(&tmap.res, a.X_in, batch, m.L, m.CP, sizeof(act_t), 128,
@@ -414,14 +392,6 @@ template <typename act_t>
 int launch_stats(const Dims& m, const act_t* X, const float* convw, int dil, int batch,
                  float2* stats, bool pdl, cudaStream_t st) {
   if constexpr (sizeof(act_t) == 2) {
-    if (m.CP == 128) {
-      // the unit decomposition the fused statistics of the MLP kernel use, so
-      // both give bit-identical statistics
-      LaunchTimer timer(kKStats, st);
-      launch_k(pdl, stats_units_kernel, dim3(batch), dim3(kStatsUnitThreads), 0, st,
-               reinterpret_cast<const __nv_bfloat16*>(X), convw, dil, m.L, m.C, 1e-3f, stats);
-      return launch_status();
-    }
     // segment length: long segments amortise the two halo rows, short ones
     // avoid dead slots when the chains are short (large dilation); pick the
     // length with the fewest load slots plus per-segment overhead
@@ -478,7 +448,6 @@ int run_forward_t(const Dims& m, const PackLayout& pl, const uint8_t* packed, in
                   uint8_t* ws, cudaStream_t st) {
   const FwdLayout f = fwd_layout(m, batch);
   float2* stats = reinterpret_cast<float2*>(ws + f.stats);
-  float2* stats_nxt = reinterpret_cast<float2*>(ws + f.stats2);
   int* status = reinterpret_cast<int*>(ws + f.status);
   act_t* xa = reinterpret_cast<act_t*>(ws + f.xa);
   act_t* xb = reinterpret_cast<act_t*>(ws + f.xb);
@@ -557,28 +526,14 @@ int run_forward_t(const Dims& m, const PackLayout& pl, const uint8_t* packed, in
     CHM_TRY(launch_status());
     }
   }
-  // block stack. With whole examples per CTA, the MLP launch of block i also
-  // computes block i+1's statistics from its output, so only the first block
-  // has a standalone statistics pass.
+  // block stack
   const int grid = std::min(n_tiles, device_sms());
-  const bool per_example = fused_stats_config(m) && per_example_pays(batch, m.L, device_sms());
-  bool have_stats = false;
   for (int i = 0; i < m.n_layers; ++i) {
     const uint8_t* lw = packed + pl.layers + pl.layer_stride * i;
     const float* convw = reinterpret_cast<const float*>(lw + pl.l_convw);
     const int dil = 1 << i;
-    if (!have_stats)
-      CHM_TRY(launch_stats<act_t>(m, xa, convw, dil, batch, stats, /*pdl=*/true, st));
-    MlpArgs a{};
-    a.per_example = per_example ? 1 : 0;
-    a.reverse = i & 1;
-    if (per_example && i + 1 < m.n_layers) {
-      const uint8_t* nlw = packed + pl.layers + pl.layer_stride * (i + 1);
-      a.stats_next = stats_nxt;
-      a.next_convw = reinterpret_cast<const float*>(nlw + pl.l_convw);
-      a.next_dil = 1 << (i + 1);
-      a.stats_part = reinterpret_cast<double2*>(ws + f.part);
-    }
+    CHM_TRY(launch_stats<act_t>(m, xa, convw, dil, batch, stats, /*pdl=*/true, st));
+    MlpArgs a;
     a.X_in = xa;
     a.X_out = xb;
     a.stats = stats;
@@ -595,8 +550,6 @@ int run_forward_t(const Dims& m, const PackLayout& pl, const uint8_t* packed, in
     a.status = status;
     CHM_TRY(launch_mlp<act_t>(m, a, grid, st));
     std::swap(xa, xb);
-    have_stats = a.stats_next != nullptr;
-    if (have_stats) std::swap(stats, stats_nxt);
   }
   // heads
   const int cph = head_cph(m);
@@ -788,7 +741,7 @@ int run_block_t(const Dims& m, int batch, int dil, const uint8_t* packed, const 
   const float* convw = reinterpret_cast<const float*>(packed + pl.l_convw);
   CHM_TRY(launch_stats<act_t>(m, xin, convw, dil, batch, stats, /*pdl=*/m.C != m.CP, st));
   const int n_tiles = static_cast<int>((rows + kTileRows - 1) / kTileRows);
-  MlpArgs a{};
+  MlpArgs a;
   a.X_in = xin;
   a.X_out = xout;
   a.stats = stats;

@@ -813,151 +813,6 @@ __global__ void __launch_bounds__(kStatsChainThreads, 2) stats_chain_kernel(
   }
 }
 
-// ---------------------------------------------------------------- stats units
-// Per-example statistics of y = w0 x[l-d] + w1 x[l] + w2 x[l+d] for bf16
-// activations with 128 channels, split into a fixed set of work units so that
-// any number of threads, in any order, produces bit-identical results (the
-// standalone kernel below and the MLP kernel's fused next-layer statistics
-// share this decomposition):
-//   * chain segments as in stats_chain_kernel: row r = rho + k d lies on chain
-//     rho; segment (kb, rho) is chain positions kb*kS .. kb*kS + kS-1 (kS =
-//     12), read with one halo row on each side; segments are numbered
-//     s = kb d + rho (s = rho when d >= L), so a segment's rows grow with s;
-//   * unit (chunk c, lane q): 4 channels [4c, 4c + 4) (8 bytes per row) and the
-//     contiguous segment block [q n_seg / 16, (q + 1) n_seg / 16);
-//   * a segment's y and y^2 are summed in fp32 in a fixed order, a unit adds
-//     its segments' sums into fp64 in ascending s, and the 512 unit partials
-//     are combined in one fixed order (stats_combine).
-// A warp covers one lane q for all 32 chunks: every load is one whole 256-byte
-// row.
-namespace su {
-constexpr int kChunks = 32;                 // 4-channel chunks of a 128-channel row
-constexpr int kLanes = 16;                  // segment blocks per example
-constexpr int kUnits = kChunks * kLanes;    // 512
-constexpr int kS = 12;                      // chain positions per segment
-__host__ __device__ constexpr int n_kb(int L, int d) { return ((L + d - 1) / d + kS - 1) / kS; }
-__host__ __device__ constexpr int n_seg(int L, int d) { return d >= L ? L : d * n_kb(L, d); }
-__host__ __device__ constexpr int seg_lo(int q, int ns) { return (int)((long long)q * ns / kLanes); }
-// first row of segment s (its centre row at chain position kb * kS)
-__host__ __device__ constexpr int seg_r0(int s, int L, int d) {
-  return d >= L ? s : (s % d) + (s / d) * kS * d;
-}
-// rows [0, need) must be final before lane q's segments can be read
-__host__ __device__ inline int lane_rows_needed(int q, int L, int d) {
-  const int ns = n_seg(L, d);
-  const int s1 = seg_lo(q + 1, ns);
-  if (s1 <= seg_lo(q, ns)) return 0;
-  const long long last = (long long)seg_r0(s1 - 1, L, d) + (long long)kS * d;  // right halo
-  return last >= L ? L : static_cast<int>(last) + 1;
-}
-}  // namespace su
-
-// fp32 conv weights of chunk c: pairs (4c, 4c+1), (4c+2, 4c+3) per tap
-struct StatsW {
-  f2 w0[2], w1[2], w2[2];
-};
-__device__ __forceinline__ StatsW stats_weights(const float* __restrict__ convw, int c, int C) {
-  constexpr int CP = 128;
-  StatsW w;
-#pragma unroll
-  for (int m = 0; m < 2; ++m) {
-    const int ch = 4 * c + 2 * m;
-    w.w0[m] = f2{ch < C ? convw[ch] : 0.f, ch + 1 < C ? convw[ch + 1] : 0.f};
-    w.w1[m] = f2{ch < C ? convw[CP + ch] : 0.f, ch + 1 < C ? convw[CP + ch + 1] : 0.f};
-    w.w2[m] = f2{ch < C ? convw[2 * CP + ch] : 0.f, ch + 1 < C ? convw[2 * CP + ch + 1] : 0.f};
-  }
-  return w;
-}
-
-// Unit (c, q) of one example: Xe points at the example's first row as 8-byte
-// chunks (32 per row). Loads go through L2 only (the rows may have been
-// written by this kernel's bulk stores).
-__device__ __forceinline__ double2 stats_unit(const uint2* __restrict__ Xe, int c, int q,
-                                              const StatsW& w, int d, int L) {
-  using namespace su;
-  const int ns = n_seg(L, d);
-  const int s1 = seg_lo(q + 1, ns);
-  double S = 0.0, Q = 0.0;
-  for (int s = seg_lo(q, ns); s < s1; ++s) {
-    const int r0 = seg_r0(s, L, d);
-    if (r0 >= L) continue;
-    uint2 v[kS + 2];                                   // rows r0 + (j - 1) d
-#pragma unroll
-    for (int j = 0; j < kS + 2; ++j) {
-      const long long r = (long long)r0 + (long long)(j - 1) * d;
-      v[j] = (r >= 0 && r < L) ? ld_cg_u2(Xe + r * kChunks + c) : make_uint2(0u, 0u);
-    }
-    f2 sy0{0.f, 0.f}, sy1{0.f, 0.f}, sq0{0.f, 0.f}, sq1{0.f, 0.f};
-#pragma unroll
-    for (int j = 1; j <= kS; ++j) {
-      if ((long long)r0 + (long long)(j - 1) * d < L) {
-        const f2 l0{__uint_as_float(v[j - 1].x << 16), __uint_as_float(v[j - 1].x & 0xFFFF0000u)};
-        const f2 l1{__uint_as_float(v[j - 1].y << 16), __uint_as_float(v[j - 1].y & 0xFFFF0000u)};
-        const f2 c0{__uint_as_float(v[j].x << 16), __uint_as_float(v[j].x & 0xFFFF0000u)};
-        const f2 c1{__uint_as_float(v[j].y << 16), __uint_as_float(v[j].y & 0xFFFF0000u)};
-        const f2 r0v{__uint_as_float(v[j + 1].x << 16), __uint_as_float(v[j + 1].x & 0xFFFF0000u)};
-        const f2 r1v{__uint_as_float(v[j + 1].y << 16), __uint_as_float(v[j + 1].y & 0xFFFF0000u)};
-        const f2 y0 = fma2(w.w0[0], l0, fma2(w.w1[0], c0, mul2(w.w2[0], r0v)));
-        const f2 y1 = fma2(w.w0[1], l1, fma2(w.w1[1], c1, mul2(w.w2[1], r1v)));
-        sy0 = f2{sy0.x + y0.x, sy0.y + y0.y};
-        sy1 = f2{sy1.x + y1.x, sy1.y + y1.y};
-        sq0 = fma2(y0, y0, sq0);
-        sq1 = fma2(y1, y1, sq1);
-      }
-    }
-    S += static_cast<double>((sy0.x + sy0.y) + (sy1.x + sy1.y));
-    Q += static_cast<double>((sq0.x + sq0.y) + (sq1.x + sq1.y));
-  }
-  return make_double2(S, Q);
-}
-
-// The fixed-order combine of an example's 512 unit partials (part[q * 32 + c])
-// by one warp; lane 0's result is the statistics (mean, rstd). kGlobal: the
-// partials are in global memory (read through L2), else in shared memory.
-template <bool kGlobal>
-__device__ __forceinline__ float2 stats_combine(const double2* part, int lane, int L, int C,
-                                                float eps) {
-  double S = 0.0, Q = 0.0;
-#pragma unroll 4
-  for (int q = 0; q < su::kLanes; ++q) {
-    const double2 p = kGlobal ? ld_cg_d2(part + q * su::kChunks + lane)
-                              : part[q * su::kChunks + lane];
-    S += p.x;
-    Q += p.y;
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    S += __shfl_xor_sync(0xffffffffu, S, o);
-    Q += __shfl_xor_sync(0xffffffffu, Q, o);
-  }
-  const double n = static_cast<double>(L) * static_cast<double>(C);
-  const double mean = S / n;
-  double var = Q / n - mean * mean;
-  if (var < 0.0) var = 0.0;
-  return make_float2(static_cast<float>(mean),
-                     static_cast<float>(1.0 / sqrt(var + static_cast<double>(eps))));
-}
-
-// Standalone statistics of bf16 activations with 128 channels (the first
-// block's input, and any launch without fused statistics): one block per
-// example, warp q = segment block, lane = chunk, one unit per thread.
-constexpr int kStatsUnitThreads = su::kLanes * 32;   // 512
-__global__ void __launch_bounds__(kStatsUnitThreads, 1) stats_units_kernel(
-    const __nv_bfloat16* __restrict__ X, const float* __restrict__ convw, int dil, int L, int C,
-    float eps, float2* __restrict__ stats) {
-  __shared__ double2 part[su::kUnits];
-  const int b = blockIdx.x, lane = threadIdx.x & 31, q = threadIdx.x >> 5;
-  const StatsW w = stats_weights(convw, lane, C);
-  griddep_wait();                          // the previous kernel's outputs are visible
-  const uint2* Xe = reinterpret_cast<const uint2*>(X + (size_t)b * L * 128);
-  part[q * su::kChunks + lane] = stats_unit(Xe, lane, q, w, dil, L);
-  __syncthreads();
-  if (q == 0) {
-    const float2 r = stats_combine<false>(part, lane, L, C, eps);
-    if (lane == 0) stats[b] = r;
-  }
-}
-
 // ============================================================== MLP
 // One Cheri Block update for 128-row tiles of the flattened (B*L) rows:
 //   A1 = bf16((conv(X) - mean) * rstd)            (built by all threads)
@@ -983,15 +838,6 @@ struct MlpArgs {
   int tpe;               // mlp_ws_kernel: 128-row tiles per example (ceil(L / 128))
   int HP;                // mlp_stream_kernel: padded hidden width
   int* status;
-  // mlp_ws_kernel, bf16 activations: whole examples per CTA and the next
-  // block's LayerNorm statistics computed from this launch's output
-  int batch;
-  int per_example;       // a CTA takes whole examples (tiles of one example in order)
-  int reverse;           // examples from the last to the first
-  float2* stats_next;    // statistics of the next block (nullptr: not computed here)
-  const float* next_convw;   // (3, CP) fp32 conv weights of the next block
-  int next_dil;
-  double2* stats_part;   // unit partials: gridDim.x * ws::kPartSlots * su::kUnits
 };
 
 template <int CP, int HP>
@@ -1774,10 +1620,7 @@ constexpr int kProducerWarps = 4, kEpilogueWarps = 8, kResidualWarps = 4;
 constexpr int kResidualWarp0 = kProducerWarps + kEpilogueWarps; // 12
 constexpr int kMmaWarp = kResidualWarp0 + kResidualWarps;       // 16
 constexpr int kTmaWarp = kMmaWarp + 1;                          // 17
-constexpr int kStatsWarp0 = kTmaWarp + 1;                       // 18
-constexpr int kStatsWarps = 2;
-constexpr int kThreads = (kStatsWarp0 + kStatsWarps) * 32;      // 640 (96 registers)
-constexpr int kPartSlots = 4;           // examples whose unit partials are in flight per CTA
+constexpr int kThreads = (kTmaWarp + 1) * 32;                   // 576
 constexpr uint32_t kResBox = 128 * 128;                         // 16 KB residual box
 constexpr uint32_t kW1 = 0;                                     // 256 x 128 bf16
 constexpr uint32_t kW2 = kW1 + kH * kC * 2;                     // 128 x 256 bf16
@@ -1804,10 +1647,7 @@ struct Layout {
   static constexpr uint32_t kBars = kConvW + 3 * kC * 4;
   static constexpr uint32_t kSlot = kBars + kNumBars * 8;
   static constexpr uint32_t kAbort = kSlot + 4;
-  // fused statistics: tiles stored, work-item counter, per-slot done counts
-  // and generations
-  static constexpr uint32_t kCtl = kAbort + 4;
-  static constexpr uint32_t kAlloc = kCtl + (2 + 2 * kPartSlots) * 4 + 1024;
+  static constexpr uint32_t kAlloc = kAbort + 4 + 1024;
   static_assert(kSlots <= kMaxSlots, "staging ring depth");
   static_assert(kAlloc <= 232448, "shared memory per block");
   static_assert(!kWide || sizeof(act_t) == 2, "wide staging is for bf16 activations");
@@ -1838,7 +1678,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
   using Lay = Layout<act_t, kWide>;
   constexpr uint32_t kBoxBytes = Lay::kBoxBytes, kBox = Lay::kBox, kSlotBytes = Lay::kSlotBytes;
   constexpr uint32_t kRes = Lay::kRes, kConvW = Lay::kConvW, kBars = Lay::kBars;
-  constexpr uint32_t kSlot = Lay::kSlot, kAbort = Lay::kAbort, kCtl = Lay::kCtl;
+  constexpr uint32_t kSlot = Lay::kSlot, kAbort = Lay::kAbort;
   constexpr int kSlots = Lay::kSlots;
   constexpr int kCPR = kBoxBytes / 16;                 // 16-byte chunks per staging row
   extern __shared__ uint8_t smem_raw[];
@@ -1847,17 +1687,8 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBars);
   uint32_t* slot = reinterpret_cast<uint32_t*>(smem + kSlot);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kAbort);
-  // fused statistics control words: tiles of this CTA whose stores have
-  // completed, next work item, per partial slot the finished-item count and
-  // the example that may use it next
-  int* ctl = reinterpret_cast<int*>(smem + kCtl);
-  volatile int* tiles_stored = ctl;
-  int* item_next = ctl + 1;
-  int* slot_done = ctl + 2;
-  volatile int* slot_gen = ctl + 2 + kPartSlots;
   const float* sConvW = reinterpret_cast<const float*>(smem + kConvW);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const bool fuse = (sizeof(act_t) == 2) && a.stats_next != nullptr && a.per_example;
   const act_t* Xi = static_cast<const act_t*>(a.X_in);
   act_t* Xo = static_cast<act_t*>(a.X_out);
   constexpr bool kTmaResidual = sizeof(act_t) == 2;
@@ -1878,12 +1709,6 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       mbar_init(&bars[i], count);
     }
     *abort_flag = 0;
-    ctl[0] = 0;
-    ctl[1] = 0;
-    for (int i = 0; i < kPartSlots; ++i) {
-      ctl[2 + i] = 0;
-      ctl[2 + kPartSlots + i] = i;
-    }
     mbar_init_fence();
   }
   {
@@ -1918,87 +1743,11 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
   const uint32_t tmem = *slot;
   const int first = blockIdx.x;
   const int stride = gridDim.x;
-  const int tpe = a.tpe;
-  // per_example: this CTA takes examples first, first + stride, ... (from the
-  // last example when `reverse`: a launch starts on the examples the previous
-  // one wrote last, still in L2), each as tpe consecutive tiles. Otherwise
-  // tiles are dealt round-robin from the last example to the first.
-  const int n_ex = a.per_example ? ((a.batch > first) ? (a.batch - first + stride - 1) / stride : 0)
-                                 : 0;
-  const int n_my = a.per_example ? n_ex * tpe
-                                 : ((a.n_tiles > first) ? (a.n_tiles - first + stride - 1) / stride
-                                                        : 0);
-  auto ex_of = [&](int k) -> int {
-    const int e = first + k * stride;
-    return a.reverse ? a.batch - 1 - e : e;
-  };
-  auto tile_of = [&](int tit) -> int {
-    if (a.per_example) {
-      const int k = tit / tpe;
-      return ex_of(k) * tpe + (tit - k * tpe);
-    }
-    return a.n_tiles - 1 - (first + tit * stride);
-  };
-
-  // Statistics of the next block (fused): work item = (example k of this CTA,
-  // segment block q) covering units (c = lane, q) of su::; claimed in order by
-  // whichever warp is free (the statistics warps from the start, the pipeline
-  // warps once their last tile is done). An item waits until the rows it reads
-  // are stored; the warp finishing an example's last item combines its 512
-  // partials in the fixed order. Partials of up to kPartSlots examples are in
-  // flight per CTA (global scratch, L2).
-  auto stats_work = [&]() {
-    if constexpr (sizeof(act_t) == 2) {
-      const StatsW w = stats_weights(a.next_convw, lane, a.C);
-      const int L = a.L, d = a.next_dil;
-      const int n_items = n_ex * su::kLanes;
-      double2* part_cta = a.stats_part + (size_t)blockIdx.x * kPartSlots * su::kUnits;
-      const uint2* Xo2 = reinterpret_cast<const uint2*>(a.X_out);
-      for (;;) {
-        int item = 0;
-        if (lane == 0) item = atomicAdd(item_next, 1);
-        item = __shfl_sync(0xffffffffu, item, 0);
-        if (item >= n_items) break;
-        const int k = item / su::kLanes, q = item - k * su::kLanes;
-        const int ps = k % kPartSlots;
-        const int need = su::lane_rows_needed(q, L, d);
-        bool ok = true;
-        const uint64_t t0 = global_ns();
-        for (uint32_t spin = 0;; ++spin) {
-          const int done_tiles = min(max(*tiles_stored - k * tpe, 0), tpe);
-          if (min(done_tiles * kTileRows, L) >= need && slot_gen[ps] == k) break;
-          if ((spin & 15u) == 15u && (*abort_flag || global_ns() - t0 > kWaitNs)) {
-            *abort_flag = 1;
-            ok = false;
-            break;
-          }
-          __nanosleep(128);
-        }
-        if (!ok) break;
-        __threadfence();          // the rows' stores (published before tiles_stored) first
-        const uint2* Xe = Xo2 + (size_t)ex_of(k) * L * su::kChunks;
-        double2* part = part_cta + ps * su::kUnits;
-        st_cg_d2(part + q * su::kChunks + lane, stats_unit(Xe, lane, q, w, d, L));
-        __threadfence_block();
-        __syncwarp();
-        int prev = 0;
-        if (lane == 0) prev = atomicAdd(&slot_done[ps], 1);
-        prev = __shfl_sync(0xffffffffu, prev, 0);
-        if (prev == su::kLanes - 1) {
-          // last item of example k: every partial is written
-          __threadfence_block();
-          const float2 st = stats_combine<true>(part, lane, L, a.C, 1e-3f);
-          if (lane == 0) {
-            a.stats_next[ex_of(k)] = st;
-            slot_done[ps] = 0;
-            __threadfence_block();
-            slot_gen[ps] = k + kPartSlots;
-          }
-          __syncwarp();
-        }
-      }
-    }
-  };
+  const int n_my = (a.n_tiles > first) ? (a.n_tiles - first + stride - 1) / stride : 0;
+  // tiles run from the last example to the first: the statistics kernel just
+  // read the last examples (still in L2), and the next one starts at the first
+  // examples, which this launch writes last
+  auto tile_of = [&](int tit) -> int { return a.n_tiles - 1 - (first + tit * stride); };
 
   if (warp < kProducerWarps) {
     // ------------------------------------------------------------ producer
@@ -2283,23 +2032,11 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
           tma_store_3d(&maps.out, sRes, 0, l0, n);        // rows past L are clipped
           tma_store_3d(&maps.out, sRes + kResBox, 64, l0, n);
           bulk_commit();
-          // fused statistics read the stored rows: publish how many tiles'
-          // stores have completed (all but the one just issued, or all)
-          auto publish = [&](int tiles) {
-            fence_proxy_async_global();
-            __threadfence();
-            *tiles_stored = tiles;
-          };
           if (it + 1 < n_my) {
             bulk_wait_read0();                            // the tile buffer is free again
             load_res(it + 1);
-            if (fuse) {
-              bulk_wait1();
-              publish(it);
-            }
           } else {
             bulk_wait0();                                 // stores complete before exit
-            if (fuse) publish(n_my);
           }
         }
       } else {
@@ -2418,7 +2155,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       }
     }
     __syncwarp();
-  } else if (warp == kTmaWarp) {
+  } else {
     // ------------------------------------------------------------ TMA warp
     if (lane == 0 && n_my > 0) {
       // staging box step k -> (tile k / kBoxes, box k % kBoxes) into slot k % kSlots
@@ -2465,13 +2202,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       }
     }
     __syncwarp();
-  } else {
-    // ------------------------------------------------------------ statistics warps
-    if (fuse) stats_work();
   }
-  // the producer, GELU and residual warps take the statistics items left once
-  // their last tile is done
-  if (fuse && warp < kMmaWarp && !*abort_flag) stats_work();
   // drain: every MMA this CTA issued has been waited on by the residual
   // warps (D2_FULL of the last tile) unless the pipeline aborted.
   tc_fence_before();

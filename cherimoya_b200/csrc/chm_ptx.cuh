@@ -165,31 +165,6 @@ __device__ __forceinline__ void bulk_wait_read0() {
 __device__ __forceinline__ void bulk_wait0() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
-// wait until at most the most recent bulk group is still pending: every
-// older group has completed (its writes performed)
-__device__ __forceinline__ void bulk_wait1() {
-  asm volatile("cp.async.bulk.wait_group 1;" ::: "memory");
-}
-// orders this thread's completed async-proxy global writes (bulk tensor
-// stores) before its later generic-proxy accesses
-__device__ __forceinline__ void fence_proxy_async_global() {
-  asm volatile("fence.proxy.async.global;" ::: "memory");
-}
-// global loads / stores cached in L2 only (data another warp of the CTA or
-// the async proxy wrote during this kernel)
-__device__ __forceinline__ uint2 ld_cg_u2(const uint2* p) {
-  uint2 v;
-  asm volatile("ld.global.cg.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
-  return v;
-}
-__device__ __forceinline__ double2 ld_cg_d2(const double2* p) {
-  double2 v;
-  asm volatile("ld.global.cg.v2.f64 {%0, %1}, [%2];" : "=d"(v.x), "=d"(v.y) : "l"(p));
-  return v;
-}
-__device__ __forceinline__ void st_cg_d2(double2* p, double2 v) {
-  asm volatile("st.global.cg.v2.f64 [%0], {%1, %2};" ::"l"(p), "d"(v.x), "d"(v.y) : "memory");
-}
 // named barrier over `count` threads (barrier 0 is __syncthreads)
 __device__ __forceinline__ void named_sync(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
