@@ -11,6 +11,7 @@ from .wrappers import ControlWrapper, ExpectedCountsWrapper, LogCountWrapper, Pr
 from .ism import (saturation_mutagenesis, sharded_saturation_mutagenesis,
                   sharded_variant_effect, variant_effect)
 from .predict import predict, rc_forward
+from . import attribution
 
 __version__ = "0.1.0"
 
@@ -18,5 +19,5 @@ __all__ = [
     "Cherimoya", "CheriBlock", "FusedDilatedConvNorm", "fused_dilated_conv_norm",
     "ControlWrapper", "ProfileWrapper", "LogCountWrapper", "ExpectedCountsWrapper",
     "saturation_mutagenesis", "variant_effect", "sharded_saturation_mutagenesis",
-    "sharded_variant_effect", "predict", "rc_forward",
+    "sharded_variant_effect", "predict", "rc_forward", "attribution",
 ]

@@ -653,7 +653,7 @@ bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) %
 size_t ism_len(const Dims& m) { return (size_t)m.n_out * m.Lout; }
 
 struct IsmLayout {
-  size_t fwd, ref_prof, ref_prob, ref_lc, mut_prof, mut_lc, total;
+  size_t fwd, ref_prof, ref_prob, ref_lc, ref_pw, mut_prof, mut_lc, total;
 };
 
 IsmLayout ism_layout(const Dims& m, int n_seqs, int mb) {
@@ -663,6 +663,7 @@ IsmLayout ism_layout(const Dims& m, int n_seqs, int mb) {
   l.ref_prof = o; o = align_up(o + (size_t)n_seqs * ism_len(m) * 4);
   l.ref_prob = o; o = align_up(o + (size_t)n_seqs * ism_len(m) * 4);
   l.ref_lc = o; o = align_up(o + (size_t)n_seqs * m.n_groups * 4);
+  l.ref_pw = o; o = align_up(o + (size_t)n_seqs * 4);
   l.mut_prof = o; o = align_up(o + (size_t)mb * ism_len(m) * 4);
   l.mut_lc = o; o = align_up(o + (size_t)mb * m.n_groups * 4);
   l.total = o;
@@ -949,6 +950,14 @@ int32_t chm_ism(const chm_model_desc* desc, const void* packed, int32_t n_seqs,
                 const int8_t* bases, int32_t start, int32_t end, int32_t mutant_batch,
                 float* d_logcount, float* jsd, void* workspace, size_t workspace_bytes,
                 chm_stream_t stream) {
+  return chm_ism_ex(desc, packed, n_seqs, bases, start, end, mutant_batch, d_logcount, jsd,
+                    nullptr, workspace, workspace_bytes, stream);
+}
+
+int32_t chm_ism_ex(const chm_model_desc* desc, const void* packed, int32_t n_seqs,
+                   const int8_t* bases, int32_t start, int32_t end, int32_t mutant_batch,
+                   float* d_logcount, float* jsd, float* d_profile_wrapper, void* workspace,
+                   size_t workspace_bytes, chm_stream_t stream) {
   CHM_TRY(validate(desc));
   if (n_seqs < 0 || !packed || !bases || !d_logcount || !jsd || !workspace || mutant_batch < 1)
     return CHM_ERR_INVALID_ARGUMENT;
@@ -965,6 +974,7 @@ int32_t chm_ism(const chm_model_desc* desc, const void* packed, int32_t n_seqs,
   float* ref_prof = reinterpret_cast<float*>(ws + il.ref_prof);
   float* ref_prob = reinterpret_cast<float*>(ws + il.ref_prob);
   float* ref_lc = reinterpret_cast<float*>(ws + il.ref_lc);
+  float* ref_pw = d_profile_wrapper ? reinterpret_cast<float*>(ws + il.ref_pw) : nullptr;
   float* mut_prof = reinterpret_cast<float*>(ws + il.mut_prof);
   float* mut_lc = reinterpret_cast<float*>(ws + il.mut_lc);
   uint8_t* fws = ws + il.fwd;
@@ -977,7 +987,7 @@ int32_t chm_ism(const chm_model_desc* desc, const void* packed, int32_t n_seqs,
   CHM_TRY(run_forward(m, pk, n_seqs, kInBases, rin, nullptr, ref_prof, ref_lc, fws, st));
   launches += g_launches;
   const int len = static_cast<int>(ism_len(m));
-  softmax_rows_kernel<<<n_seqs, 256, 0, st>>>(ref_prof, ref_prob, len);
+  softmax_rows_kernel<<<n_seqs, 256, 0, st>>>(ref_prof, ref_prob, len, ref_pw);
   CHM_TRY(launch_status());
   const int W = end - start;
   const long long total = (long long)n_seqs * W * 3;
@@ -1007,6 +1017,8 @@ int32_t chm_ism(const chm_model_desc* desc, const void* packed, int32_t n_seqs,
     sa.L = m.L;
     sa.d_logcount = d_logcount;
     sa.jsd = jsd;
+    sa.pw_ref = ref_pw;
+    sa.d_pw = d_profile_wrapper;
     {
       LaunchTimer timer(kKScore, st);
       score_kernel<<<nb, 256, 0, st>>>(sa);
@@ -1018,7 +1030,8 @@ int32_t chm_ism(const chm_model_desc* desc, const void* packed, int32_t n_seqs,
     const long long n = (long long)n_seqs * W;
     ism_fill_ref_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(bases, m.L, start, W,
                                                                      m.n_groups, n_seqs,
-                                                                     d_logcount, jsd);
+                                                                     d_logcount, jsd,
+                                                                     d_profile_wrapper);
     CHM_TRY(launch_status());
     launches += 2;
   }
@@ -1067,7 +1080,7 @@ int32_t chm_variant(const chm_model_desc* desc, const void* packed, int32_t n_pa
     g_launches = 0;
     CHM_TRY(run_forward(m, pk, nb, kInBases, ain, nullptr, alt_prof, alt_lc, fws, st));
     launches += g_launches;
-    softmax_rows_kernel<<<nb, 256, 0, st>>>(ref_prof, ref_prob, len);
+    softmax_rows_kernel<<<nb, 256, 0, st>>>(ref_prof, ref_prob, len, nullptr);
     CHM_TRY(launch_status());
     ScoreArgs sa{};
     sa.logits = alt_prof;

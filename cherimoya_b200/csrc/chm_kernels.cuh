@@ -2850,9 +2850,14 @@ __global__ void __launch_bounds__(hd3::kThreads, 1) head_fused_kernel(
 }
 
 // ============================================================== scoring
-// Row-wise softmax of a reference profile flattened over (n_out, Lout).
+// Row-wise softmax of a reference profile flattened over (n_out, Lout), and
+// (pw != nullptr) the row's ProfileWrapper value
+//   sum_i softmax(x)_i (x_i - mean(x)) = sum_i softmax(x)_i x_i - mean(x)
+// (upstream wrappers.py:71-99: mean-centred flattened logits weighted by
+// their softmax, which the centring does not change).
 __global__ void __launch_bounds__(256) softmax_rows_kernel(const float* __restrict__ logits,
-                                                           float* __restrict__ probs, int len) {
+                                                           float* __restrict__ probs, int len,
+                                                           float* __restrict__ pw) {
   __shared__ float red[8];
   __shared__ float bcast;
   const long long base = (long long)blockIdx.x * len;
@@ -2884,8 +2889,34 @@ __global__ void __launch_bounds__(256) softmax_rows_kernel(const float* __restri
   }
   __syncthreads();
   const float inv = 1.0f / bcast;
-  for (int i = threadIdx.x; i < len; i += blockDim.x)
-    probs[base + i] = expf(logits[base + i] - m) * inv;
+  float sx = 0.f, spx = 0.f;
+  for (int i = threadIdx.x; i < len; i += blockDim.x) {
+    const float x = logits[base + i];
+    const float p = expf(x - m) * inv;
+    probs[base + i] = p;
+    sx += x;
+    spx = fmaf(p, x, spx);
+  }
+  if (pw == nullptr) return;
+  __shared__ float red2[2][8];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    sx += __shfl_xor_sync(0xffffffffu, sx, o);
+    spx += __shfl_xor_sync(0xffffffffu, spx, o);
+  }
+  if (lane == 0) {
+    red2[0][warp] = sx;
+    red2[1][warp] = spx;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float tx = 0.f, tp = 0.f;
+    for (int i = 0; i < 8; ++i) {
+      tx += red2[0][i];
+      tp += red2[1][i];
+    }
+    pw[blockIdx.x] = tp - tx / static_cast<float>(len);
+  }
 }
 
 // Jensen-Shannon distance between softmax(logits[i]) and probs[ref_of(i)]
@@ -2912,6 +2943,8 @@ struct ScoreArgs {
   int L;
   float* d_logcount;        // ISM: (n_ref, n_groups, 4, W); variant: (n, n_groups)
   float* jsd;               // ISM: (n_ref, 4, W); variant: (n)
+  const float* pw_ref;      // ISM, optional: ProfileWrapper value of each reference
+  float* d_pw;              // ISM, optional: (n_ref, 4, W) its change in the mutant
 };
 
 __global__ void __launch_bounds__(256) score_kernel(ScoreArgs a) {
@@ -2950,21 +2983,36 @@ __global__ void __launch_bounds__(256) score_kernel(ScoreArgs a) {
   }
   __syncthreads();
   const float inv = 1.0f / bcast;
-  float j = 0.f;
+  // JSD terms, and for the ProfileWrapper value sum(x) and sum(softmax * x)
+  float j = 0.f, sx = 0.f, spx = 0.f;
   for (int i = threadIdx.x; i < a.len; i += blockDim.x) {
     const float p1 = expf(x[i] - m) * inv;
     const float p2 = q[i];
     const float mid = 0.5f * (p1 + p2);
     j += kl_term(p1, mid) + kl_term(p2, mid);
+    sx += x[i];
+    spx = fmaf(p1, x[i], spx);
   }
+  __shared__ float red3[3][8];
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) j += __shfl_xor_sync(0xffffffffu, j, o);
-  __syncthreads();
-  if (lane == 0) red[warp] = j;
+  for (int o = 16; o > 0; o >>= 1) {
+    j += __shfl_xor_sync(0xffffffffu, j, o);
+    sx += __shfl_xor_sync(0xffffffffu, sx, o);
+    spx += __shfl_xor_sync(0xffffffffu, spx, o);
+  }
+  if (lane == 0) {
+    red3[0][warp] = j;
+    red3[1][warp] = sx;
+    red3[2][warp] = spx;
+  }
   __syncthreads();
   if (threadIdx.x != 0) return;
-  float jt = 0.f;
-  for (int i = 0; i < 8; ++i) jt += red[i];
+  float jt = 0.f, tx = 0.f, tp = 0.f;
+  for (int i = 0; i < 8; ++i) {
+    jt += red3[0][i];
+    tx += red3[1][i];
+    tp += red3[2][i];
+  }
   jt *= 0.5f;
   if (a.ism) {
     const int rem = static_cast<int>(gm - (long long)ref * a.per_ref);
@@ -2972,6 +3020,9 @@ __global__ void __launch_bounds__(256) score_kernel(ScoreArgs a) {
     const int p = a.ism_start + w;
     const int alt = ((a.bases[(long long)ref * a.L + p] & 3) + 1 + k) & 3;
     a.jsd[((long long)ref * 4 + alt) * a.ism_width + w] = jt;
+    if (a.d_pw)
+      a.d_pw[((long long)ref * 4 + alt) * a.ism_width + w] =
+          (tp - tx / static_cast<float>(a.len)) - a.pw_ref[ref];
     for (int g = 0; g < a.n_groups; ++g) {
       const float d = a.lc[(long long)row * a.n_groups + g] - a.lc_ref[(long long)ref * a.n_groups + g];
       a.d_logcount[(((long long)ref * a.n_groups + g) * 4 + alt) * a.ism_width + w] = d;
@@ -2987,12 +3038,14 @@ __global__ void __launch_bounds__(256) score_kernel(ScoreArgs a) {
 // ISM entries whose base equals the reference base: the mutant is the
 // reference, both scores are 0.
 __global__ void ism_fill_ref_kernel(const int8_t* __restrict__ bases, int L, int start, int W,
-                                    int n_groups, int n_ref, float* d_logcount, float* jsd) {
+                                    int n_groups, int n_ref, float* d_logcount, float* jsd,
+                                    float* d_pw) {
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (long long)n_ref * W) return;
   const int n = static_cast<int>(i / W), w = static_cast<int>(i - (long long)n * W);
   const int b = bases[(long long)n * L + start + w] & 3;
   jsd[((long long)n * 4 + b) * W + w] = 0.f;
+  if (d_pw) d_pw[((long long)n * 4 + b) * W + w] = 0.f;
   for (int g = 0; g < n_groups; ++g)
     d_logcount[(((long long)n * n_groups + g) * 4 + b) * W + w] = 0.f;
 }

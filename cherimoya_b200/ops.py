@@ -212,6 +212,45 @@ def _ism_fake(bases, start, end, mutant_batch, packed, packed_offset, desc, resi
             bases.new_empty((N, 4, W), dtype=torch.float32))
 
 
+@torch.library.custom_op("cherimoya_b200::ism_targets", mutates_args=())
+def ism_targets(bases: torch.Tensor, start: int, end: int, mutant_batch: int,
+                packed: torch.Tensor, packed_offset: int, desc: List[int],
+                residual_scale: float) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """ism() plus the change of the ProfileWrapper value in every mutant:
+    d_logcount (N, n_groups, 4, W), jsd (N, 4, W), d_profile_wrapper (N, 4, W)."""
+    lib = _lib.load()
+    _require_cuda(bases, "bases")
+    if bases.dim() != 2 or bases.shape[1] != desc[D_L]:
+        raise RuntimeError("cherimoya_b200: expected bases of shape (N, L)")
+    if not (0 <= start < end <= desc[D_L]):
+        raise RuntimeError("cherimoya_b200: invalid ISM window [{}, {})".format(start, end))
+    bases = bases.to(torch.int8).contiguous()
+    N, W = bases.shape[0], end - start
+    dlc = torch.empty(N, desc[D_NG], 4, W, dtype=torch.float32, device=bases.device)
+    jsd = torch.empty(N, 4, W, dtype=torch.float32, device=bases.device)
+    dpw = torch.empty(N, 4, W, dtype=torch.float32, device=bases.device)
+    if N == 0:
+        return dlc, jsd, dpw
+    d = _desc(desc, residual_scale)
+    mb = max(1, int(mutant_batch))
+    nbytes = lib.chm_ism_workspace_bytes(ctypes.byref(d), N, mb)
+    ws, off = aligned_empty(nbytes, bases.device)
+    st = lib.chm_ism_ex(ctypes.byref(d), ctypes.c_void_p(packed.data_ptr() + packed_offset), N,
+                        _ptr(bases), int(start), int(end), mb, _ptr(dlc), _ptr(jsd), _ptr(dpw),
+                        ctypes.c_void_p(ws.data_ptr() + off), nbytes, _stream(bases.device))
+    _lib.check(st, "ism_targets")
+    return dlc, jsd, dpw
+
+
+@ism_targets.register_fake
+def _ism_targets_fake(bases, start, end, mutant_batch, packed, packed_offset, desc,
+                      residual_scale):
+    N, W = bases.shape[0], end - start
+    return (bases.new_empty((N, desc[D_NG], 4, W), dtype=torch.float32),
+            bases.new_empty((N, 4, W), dtype=torch.float32),
+            bases.new_empty((N, 4, W), dtype=torch.float32))
+
+
 @torch.library.custom_op("cherimoya_b200::variant", mutates_args=())
 def variant(ref_bases: torch.Tensor, alt_bases: torch.Tensor, packed: torch.Tensor,
             packed_offset: int, desc: List[int],

@@ -144,6 +144,19 @@ int32_t chm_ism(const chm_model_desc* desc, const void* packed, int32_t n_seqs,
                 float* d_logcount, float* jsd,
                 void* workspace, size_t workspace_bytes, chm_stream_t stream);
 
+/* chm_ism plus, when d_profile_wrapper is not null, the change of the
+ * ProfileWrapper value (upstream cherimoya/wrappers.py:71-99: the flattened
+ * profile logits, mean-centred, weighted by their softmax and summed) in
+ * every mutant, (n_seqs, 4, end - start), 0 at the reference base. With
+ * d_logcount (group g) this is the scalar each upstream attribution target
+ * (LogCountWrapper / ProfileWrapper over ControlWrapper, the two outputs of
+ * cherimoya_cli/commands/attribute.py:46-51) takes in the mutant minus in the
+ * reference. Same workspace as chm_ism. */
+int32_t chm_ism_ex(const chm_model_desc* desc, const void* packed, int32_t n_seqs,
+                   const int8_t* bases, int32_t start, int32_t end, int32_t mutant_batch,
+                   float* d_logcount, float* jsd, float* d_profile_wrapper,
+                   void* workspace, size_t workspace_bytes, chm_stream_t stream);
+
 /* Workspace bytes chm_variant needs for n_pairs pairs. */
 size_t chm_variant_workspace_bytes(const chm_model_desc* desc, int32_t n_pairs);
 

@@ -228,6 +228,37 @@ def ism_scores(sd, config, bases, start, end, batch=256):
     return dlc, jsd, p_ref, c_ref
 
 
+def ism_wrapper_deltas(sd, config, bases, start, end, kind, target=0, batch=256):
+    """Change of an attribution target's scalar in every single-base mutant
+    of positions [start, end) (the targets of the upstream attribute command,
+    cherimoya_cli/commands/attribute.py:46-51): kind "logcount" -> the
+    LogCountWrapper output column `target` (wrappers.py:102-122), kind
+    "profile" -> the ProfileWrapper value (wrappers.py:71-99), each through a
+    ControlWrapper (zero controls, wrappers.py:38-47). Returns (N, 4, W):
+    y(reference with base b at p) - y(reference), by explicit mutant
+    forwards."""
+    def y(X):
+        p, c = forward(sd, config, X, control_inputs(config, X))
+        return c[:, target] if kind == "logcount" else profile_wrapper(p)[:, 0]
+
+    X = one_hot(bases)
+    N, _, L = X.shape
+    W = end - start
+    out = torch.zeros(N, 4, W)
+    with torch.no_grad():
+        y_ref = y(X)
+        pos = torch.arange(start, end).repeat_interleave(4)
+        alt = torch.arange(4).repeat(W)
+        for n in range(N):
+            for s in range(0, 4 * W, batch):
+                pp, aa = pos[s:s + batch], alt[s:s + batch]
+                Xm = X[n].unsqueeze(0).repeat(len(pp), 1, 1)
+                Xm[torch.arange(len(pp)), :, pp] = 0.0
+                Xm[torch.arange(len(pp)), aa, pp] = 1.0
+                out[n, aa, pp - start] = y(Xm) - y_ref[n]
+    return out
+
+
 def variant_scores(sd, config, ref_bases, alt_bases):
     """Ref/alt variant-effect scoring (the pattern of the upstream tutorial
     docs/tutorials/variant_effect.rst:50-69: predict both, take the delta).
