@@ -27,6 +27,12 @@ reference's pure-PyTorch path, imported from baseline/_ref by
 oracle/upstream.py; the oracle port when that install is absent) on the
 same workload, a bounded sample of sequences per step, on rank 0 only.
 
+--impl reference-gpu (opt-in, not part of the default runs) times the
+upstream package's own CUDA inference path on this GPU: its Triton fused
+Cheri Block kernels (upstream cherimoya/cheri.py:490-754) under
+torch.no_grad(), compile=False, bf16 autocast, same weights and inputs,
+inputs resident on the device.
+
 --workload selects the model and input set (the default is the one above):
   forward    default 9-layer model, uniform random sequences, batch 1024
   multitask  the same backbone with 1 unstranded + 4 stranded tracks
@@ -310,6 +316,56 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_reference_gpu(args, world, rank, local):
+    """--impl reference-gpu: the upstream package's Triton inference path on
+    this GPU (rank 0 only), device-resident inputs, CUDA-event timing."""
+    if rank != 0:
+        return
+    import torch
+    from oracle import upstream
+    from oracle.cherimoya_oracle import one_hot
+    if not upstream.available():
+        print(json.dumps({"impl": "reference-gpu",
+                          "unavailable": "upstream package not installed in baseline/_ref"}))
+        return
+    ref = upstream.import_upstream()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    m = build_model(args)
+    cfg = m._init_kwargs()
+    um = ref.Cherimoya(**cfg, compile=False)
+    um.load_state_dict(m.state_dict())
+    um = um.eval().to(dev)
+    seed = WORKLOADS[args.workload][2]
+    X = one_hot(make_bases(args.workload, args.batch, seed)[0]).to(dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    amp = torch.autocast("cuda", dtype=torch.bfloat16, enabled=args.mode == "bf16")
+    with torch.no_grad(), amp:
+        for _ in range(max(args.warmup, 3)):
+            um(X)
+        torch.cuda.synchronize()
+        ms = []
+        for _ in range(args.steps):
+            flush.zero_()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            um(X)
+            e1.record()
+            torch.cuda.synchronize()
+            ms.append(e0.elapsed_time(e1))
+    total = sum(ms)
+    line = {
+        "impl": "reference-gpu", "metric": METRIC, "value": args.batch * args.steps / (total / 1e3),
+        "unit": WORKLOADS[args.workload][3], "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": total / args.steps, "higher_is_better": True,
+        "dtype": args.mode, "data": "synthetic", "config": workload_config(args, 1),
+        "what": "upstream cherimoya 0.2.1 Cherimoya.forward on CUDA (Triton fused Cheri Block "
+                "inference kernels), no_grad, compile=False, {} autocast".format(args.mode),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def workload_config(args, world):
     if args.workload == "multitask":
         what = ("9-layer Cherimoya forward, signal_groups [1, 2, 2, 2, 2] (9 profile tracks, "
@@ -572,7 +628,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", "1")))
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "reference-gpu"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="forward")
     ap.add_argument("--batch", type=int, default=None,
                     help="units per GPU per step (default: the workload's)")
@@ -590,6 +646,8 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
+        elif args.impl == "reference-gpu":
+            run_reference_gpu(args, world, rank, local)
         else:
             run_ours(args, world, rank, local)
     finally:
