@@ -21,8 +21,8 @@ ABI_VERSION = 1
 EXPORTED = (
     "chm_abi_version", "chm_error_string", "chm_validate", "chm_packed_weights_bytes",
     "chm_pack_weights", "chm_forward_workspace_bytes", "chm_forward", "chm_forward_bases",
-    "chm_ism_workspace_bytes", "chm_ism", "chm_ism_ex", "chm_variant_workspace_bytes",
-    "chm_variant",
+    "chm_ism_workspace_bytes", "chm_ism", "chm_ism_ex", "chm_wrapper_epilogue",
+    "chm_variant_workspace_bytes", "chm_variant",
     "chm_block_packed_bytes", "chm_pack_block", "chm_block_workspace_bytes",
     "chm_block_forward", "chm_forward_noalloc", "chm_noalloc_read_status", "chm_read_status",
     "chm_last_launch_count", "chm_timing_enable", "chm_timing_collect",
@@ -83,6 +83,7 @@ def _declare(lib):
         "chm_ism_workspace_bytes": (sz, [desc_p, i32, i32]),
         "chm_ism": (i32, [desc_p, vp, i32, vp, i32, i32, i32, vp, vp, vp, sz, vp]),
         "chm_ism_ex": (i32, [desc_p, vp, i32, vp, i32, i32, i32, vp, vp, vp, vp, sz, vp]),
+        "chm_wrapper_epilogue": (i32, [desc_p, i32, vp, vp, vp, vp, vp, vp, sz, vp]),
         "chm_variant_workspace_bytes": (sz, [desc_p, i32]),
         "chm_variant": (i32, [desc_p, vp, i32, vp, vp, vp, vp, vp, sz, vp]),
         "chm_block_packed_bytes": (sz, [i32, i32]),

@@ -1039,6 +1039,39 @@ int32_t chm_ism_ex(const chm_model_desc* desc, const void* packed, int32_t n_seq
   return CHM_OK;
 }
 
+int32_t chm_wrapper_epilogue(const chm_model_desc* desc, int32_t batch, const float* profile,
+                             const float* logcounts, const int32_t* group_sizes,
+                             float* expected_counts, float* profile_wrapper,
+                             void* workspace, size_t workspace_bytes, chm_stream_t stream) {
+  CHM_TRY(validate(desc));
+  if (batch < 0 || !profile || !logcounts) return CHM_ERR_INVALID_ARGUMENT;
+  if (batch == 0) return CHM_OK;
+  const Dims m = dims_of(desc);
+  const size_t len = (size_t)m.n_out * m.Lout;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (expected_counts) {
+    if (!group_sizes || m.n_groups > kMaxEpilogueGroups) return CHM_ERR_INVALID_ARGUMENT;
+    GroupOffsets go{};
+    for (int g = 0; g < m.n_groups; ++g) {
+      if (group_sizes[g] < 1) return CHM_ERR_INVALID_ARGUMENT;
+      go.off[g + 1] = go.off[g] + group_sizes[g];
+    }
+    if (go.off[m.n_groups] != m.n_out) return CHM_ERR_INVALID_ARGUMENT;
+    expected_counts_kernel<<<dim3(m.n_groups, batch), 256, 0, st>>>(
+        profile, logcounts, m.n_out, m.Lout, m.n_groups, go, expected_counts);
+    CHM_TRY(launch_status());
+  }
+  if (profile_wrapper) {
+    // the softmax itself goes to the caller's workspace (batch * len floats)
+    if (!workspace || workspace_bytes < (size_t)batch * len * sizeof(float))
+      return CHM_ERR_WORKSPACE;
+    softmax_rows_kernel<<<batch, 256, 0, st>>>(profile, static_cast<float*>(workspace),
+                                               static_cast<int>(len), profile_wrapper);
+    CHM_TRY(launch_status());
+  }
+  return CHM_OK;
+}
+
 size_t chm_variant_workspace_bytes(const chm_model_desc* desc, int32_t n_pairs) {
   if (validate(desc) != CHM_OK || n_pairs < 1) return 0;
   return var_layout(dims_of(desc), n_pairs).total;

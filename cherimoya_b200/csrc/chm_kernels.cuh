@@ -2919,6 +2919,53 @@ __global__ void __launch_bounds__(256) softmax_rows_kernel(const float* __restri
   }
 }
 
+// ExpectedCountsWrapper (upstream wrappers.py:125-166): for example n and
+// signal group g (channels [off[g], off[g + 1]) of the profile), a joint softmax
+// over the group's channels and positions times expm1(logcount[n, g]).
+constexpr int kMaxEpilogueGroups = 64;
+struct GroupOffsets {
+  int off[kMaxEpilogueGroups + 1];
+};
+__global__ void __launch_bounds__(256) expected_counts_kernel(
+    const float* __restrict__ profile, const float* __restrict__ logcounts, int n_out, int Lout,
+    int n_groups, GroupOffsets go, float* __restrict__ out) {
+  __shared__ float red[8];
+  __shared__ float bcast;
+  const int g = blockIdx.x, n = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long base = ((long long)n * n_out + go.off[g]) * Lout;
+  const int len = (go.off[g + 1] - go.off[g]) * Lout;
+  float m = -INFINITY;
+  for (int i = threadIdx.x; i < len; i += blockDim.x) m = fmaxf(m, profile[base + i]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = red[0];
+    for (int i = 1; i < 8; ++i) t = fmaxf(t, red[i]);
+    bcast = t;
+  }
+  __syncthreads();
+  m = bcast;
+  float s = 0.f;
+  for (int i = threadIdx.x; i < len; i += blockDim.x) s += expf(profile[base + i] - m);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  __syncthreads();
+  if (lane == 0) red[warp] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int i = 0; i < 8; ++i) t += red[i];
+    bcast = t;
+  }
+  __syncthreads();
+  const float scale = expm1f(logcounts[(long long)n * n_groups + g]) / bcast;
+  for (int i = threadIdx.x; i < len; i += blockDim.x)
+    out[base + i] = expf(profile[base + i] - m) * scale;
+}
+
 // Jensen-Shannon distance between softmax(logits[i]) and probs[ref_of(i)]
 // over `len` values (upstream performance.py:138-207: zero-probability
 // terms contribute 0, natural log), plus the log-count delta of every

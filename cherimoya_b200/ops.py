@@ -251,6 +251,68 @@ def _ism_targets_fake(bases, start, end, mutant_batch, packed, packed_offset, de
             bases.new_empty((N, 4, W), dtype=torch.float32))
 
 
+# ----------------------------------------------------------------- wrapper epilogues
+def _epilogue_desc(profile, n_groups):
+    # only n_outputs, n_groups and the output length matter to the epilogues
+    N, n_out, Lout = profile.shape
+    return _lib.make_desc(128, 0, 1, n_out, n_groups, 0, 0, Lout, 0.0, _lib.MODE_FP32)
+
+
+@torch.library.custom_op("cherimoya_b200::expected_counts", mutates_args=())
+def expected_counts(profile: torch.Tensor, logcounts: torch.Tensor,
+                    group_sizes: List[int]) -> torch.Tensor:
+    """ExpectedCountsWrapper's output from a forward's (profile, logcounts):
+    per signal group a joint softmax over its channels and positions times
+    expm1(logcount), one fused kernel."""
+    lib = _lib.load()
+    _require_cuda(profile, "profile")
+    profile = profile.float().contiguous()
+    logcounts = logcounts.to(device=profile.device, dtype=torch.float32).contiguous()
+    if profile.dim() != 3 or logcounts.shape != (profile.shape[0], len(group_sizes)) or \
+            sum(group_sizes) != profile.shape[1]:
+        raise RuntimeError("cherimoya_b200: expected_counts shape mismatch")
+    out = torch.empty_like(profile)
+    if profile.shape[0] == 0:
+        return out
+    d = _epilogue_desc(profile, len(group_sizes))
+    gs = (ctypes.c_int32 * len(group_sizes))(*[int(g) for g in group_sizes])
+    st = lib.chm_wrapper_epilogue(ctypes.byref(d), profile.shape[0], _ptr(profile),
+                                  _ptr(logcounts), gs, _ptr(out), None, None, 0,
+                                  _stream(profile.device))
+    _lib.check(st, "expected_counts")
+    return out
+
+
+@expected_counts.register_fake
+def _expected_counts_fake(profile, logcounts, group_sizes):
+    return torch.empty_like(profile, dtype=torch.float32)
+
+
+@torch.library.custom_op("cherimoya_b200::profile_wrapper", mutates_args=())
+def profile_wrapper(profile: torch.Tensor) -> torch.Tensor:
+    """ProfileWrapper's output (N, 1) from profile logits (N, n_out, Lout)."""
+    lib = _lib.load()
+    _require_cuda(profile, "profile")
+    profile = profile.float().contiguous()
+    if profile.dim() != 3:
+        raise RuntimeError("cherimoya_b200: profile_wrapper expects (N, n_out, L)")
+    N = profile.shape[0]
+    out = torch.empty(N, 1, dtype=torch.float32, device=profile.device)
+    if N == 0:
+        return out
+    d = _epilogue_desc(profile, 1)
+    ws = torch.empty_like(profile)            # the softmax, not returned
+    st = lib.chm_wrapper_epilogue(ctypes.byref(d), N, _ptr(profile), _ptr(profile), None, None,
+                                  _ptr(out), _ptr(ws), ws.numel() * 4, _stream(profile.device))
+    _lib.check(st, "profile_wrapper")
+    return out
+
+
+@profile_wrapper.register_fake
+def _profile_wrapper_fake(profile):
+    return profile.new_empty((profile.shape[0], 1), dtype=torch.float32)
+
+
 @torch.library.custom_op("cherimoya_b200::variant", mutates_args=())
 def variant(ref_bases: torch.Tensor, alt_bases: torch.Tensor, packed: torch.Tensor,
             packed_offset: int, desc: List[int],

@@ -1,9 +1,19 @@
 """Output wrappers, drop-in for upstream ``cherimoya/wrappers.py``.
 
-They call ``model(...)``, so on CUDA under ``no_grad`` they run the engine.
+They call ``model(...)``, so on CUDA under ``no_grad`` they run the engine;
+there the ProfileWrapper and ExpectedCountsWrapper arithmetic on the
+forward's outputs also runs as one fused kernel each (``ops.profile_wrapper``,
+``ops.expected_counts``).
 """
 
 import torch
+
+
+def _engine_epilogue(profile):
+    """The fused epilogue kernels serve CUDA inference on fp32 outputs (what
+    the engine's forward returns); anything else keeps the PyTorch ops."""
+    return (profile.is_cuda and not torch.is_grad_enabled() and profile.dtype == torch.float32
+            and profile.dim() == 3)
 
 
 class ControlWrapper(torch.nn.Module):
@@ -47,7 +57,11 @@ class ProfileWrapper(torch.nn.Module):
         self.scaling = _ProfileLogitScaling()
 
     def forward(self, X, X_ctl=None):
-        logits = self.flatten(self.model(X, X_ctl=X_ctl)[0])
+        profile = self.model(X, X_ctl=X_ctl)[0]
+        if _engine_epilogue(profile):
+            from . import ops
+            return ops.profile_wrapper(profile)
+        logits = self.flatten(profile)
         logits = logits - torch.mean(logits, dim=-1, keepdims=True)
         return self.scaling(logits).sum(dim=-1, keepdims=True)
 
@@ -73,6 +87,9 @@ class ExpectedCountsWrapper(torch.nn.Module):
 
     def forward(self, X, X_ctl=None):
         y_logits, y_logcounts = self.model(X, X_ctl=X_ctl)
+        if _engine_epilogue(y_logits):
+            from . import ops
+            return ops.expected_counts(y_logits, y_logcounts, list(self.model.signal_groups))
         y_counts = torch.expm1(y_logcounts)
         out = []
         for i, logits in enumerate(torch.split(y_logits, self.model.signal_groups, dim=1)):

@@ -157,6 +157,21 @@ int32_t chm_ism_ex(const chm_model_desc* desc, const void* packed, int32_t n_seq
                    float* d_logcount, float* jsd, float* d_profile_wrapper,
                    void* workspace, size_t workspace_bytes, chm_stream_t stream);
 
+/* Output-wrapper epilogues on a forward's outputs (profile (batch, n_outputs,
+ * L - 2T) and logcounts (batch, n_groups), fp32, device):
+ *   expected_counts (same shape as profile; skipped when null): per signal group
+ *     (group_sizes: n_groups host ints summing to n_outputs) a joint softmax over
+ *     the group's channels and positions times expm1(logcount) -- upstream
+ *     ExpectedCountsWrapper, cherimoya/wrappers.py:125-166;
+ *   profile_wrapper (batch floats; skipped when null): the flattened logits,
+ *     mean-centred, weighted by their softmax and summed -- upstream
+ *     ProfileWrapper, cherimoya/wrappers.py:71-99; needs a workspace of
+ *     batch * n_outputs * (L - 2T) floats. */
+int32_t chm_wrapper_epilogue(const chm_model_desc* desc, int32_t batch, const float* profile,
+                             const float* logcounts, const int32_t* group_sizes,
+                             float* expected_counts, float* profile_wrapper,
+                             void* workspace, size_t workspace_bytes, chm_stream_t stream);
+
 /* Workspace bytes chm_variant needs for n_pairs pairs. */
 size_t chm_variant_workspace_bytes(const chm_model_desc* desc, int32_t n_pairs);
 

@@ -138,3 +138,23 @@ def test_batch1024_bf16_rows_against_oracle(golden):
         rp, rc = O.forward(case["state_dict"], case["config"], O.one_hot(bases[rows]))
     _check("bf16", p.cpu()[rows], c.cpu()[rows], rp, rc, "batch1024")
     assert torch.isfinite(p).all() and torch.isfinite(c).all()
+
+
+def test_wrapper_epilogue_kernels_against_oracle():
+    """The fused ExpectedCountsWrapper / ProfileWrapper kernels on random
+    logits (grouped, 9 tracks) against the oracle's restatement of upstream
+    wrappers.py:71-99, 125-166: fp32, relative error <= 1e-5."""
+    from cherimoya_b200 import ops
+    g = torch.Generator().manual_seed(7)
+    p = torch.randn(5, 9, 1000, generator=g) * 3.0
+    c = torch.randn(5, 5, generator=g)
+    groups = [1, 2, 2, 2, 2]
+    e = ops.expected_counts(p.to(DEV), c.to(DEV), groups).cpu()
+    pw = ops.profile_wrapper(p.to(DEV)).cpu()
+    ref_e = O.expected_counts(p, c, groups)
+    ref_pw = O.profile_wrapper(p)
+    assert e.shape == ref_e.shape and pw.shape == ref_pw.shape
+    rel_e = ((e - ref_e).abs() / (ref_e.abs() + 1e-30)).max().item()
+    rel_pw = ((pw - ref_pw).abs() / ref_pw.abs().clamp_min(1e-3)).max().item()
+    print("epilogues: expected counts rel %.2e, profile wrapper rel %.2e" % (rel_e, rel_pw))
+    assert rel_e <= 1e-5 and rel_pw <= 1e-5
