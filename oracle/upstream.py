@@ -7,9 +7,9 @@ upstream CPU forward timed on the host cores) and by the fixture generator
 Where the package is looked up, first match wins:
   1. ``$CHERIMOYA_REFERENCE`` -- a source checkout (a directory holding
      ``cherimoya/``) or a pip ``--target`` directory;
-  2. ``baseline/_ref`` under the repository root, the pip install made with
-     ``python -m pip install --no-index --no-build-isolation --no-deps
-     --find-links /opt/wheelhouse --target baseline/_ref <checkout>``.
+  2. ``baseline/_ref`` under the repository root, a pip ``--target`` install
+     of the upstream checkout (``--no-deps``: its third-party imports are
+     replaced below).
 
 The upstream package imports two third-party projects at module import time
 that are not installed here: ``tangermeme`` (``predict``,
