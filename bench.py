@@ -366,6 +366,51 @@ def run_reference_gpu(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+def time_other_workload(name, args, world, rank, dev, steps=5, warmup=3):
+    """Device-resident throughput of another workload's step (per GPU batch
+    of that workload, weak scaling, max over ranks): the multi-task backbone
+    (seq/s) and the 12-layer n_filters-256 variant scoring (pairs/s)."""
+    import copy
+    import torch
+    import cherimoya_b200 as cb
+    from oracle.cherimoya_oracle import one_hot  # input generator only
+    wargs = copy.copy(args)
+    wargs.workload = name
+    batch = WORKLOADS[name][1]
+    wargs.batch = batch
+    model = build_model(wargs).eval().to(dev)
+    xs = [one_hot(b).to(dev) for b in make_bases(name, batch, WORKLOADS[name][2] + rank)]
+
+    def step():
+        if name == "variant":
+            return cb.variant_effect(model, xs[0], xs[1])
+        return model(xs[0])
+
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    with torch.no_grad():
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize()
+        barrier(world)
+        ms = 0.0
+        for _ in range(steps):
+            flush.zero_()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            step()
+            e1.record()
+            torch.cuda.synchronize()
+            ms += e0.elapsed_time(e1)
+        barrier(world)
+    ms = max_over_ranks(ms, world, dev)
+    del model, xs, flush
+    torch.cuda.empty_cache()
+    return {"value": world * batch * steps / (ms / 1000.0), "unit": WORKLOADS[name][3],
+            "ms_per_step": ms / steps, "steps": steps, "batch_per_gpu": batch,
+            "workload": workload_config(wargs, world)["workload"]}
+
+
 def workload_config(args, world):
     if args.workload == "multitask":
         what = ("9-layer Cherimoya forward, signal_groups [1, 2, 2, 2, 2] (9 profile tracks, "
@@ -567,6 +612,13 @@ def run_ours(args, world, rank, local):
                                "per mutant, {} mode; H2D of bases, all-gather and D2H of the "
                                "scores inside the timed region".format(n_seq, world, args.mode)}
 
+        # ---- the multi-task and variant-scoring configurations, a few
+        # device-resident steps each (part of the default forward run)
+        others = None
+        if args.workload == "forward" and not args.no_other_configs:
+            others = {name: time_other_workload(name, args, world, rank, dev)
+                      for name in ("multitask", "variant")}
+
         # ---- variant scoring of --variant-pairs ref/alt pairs in total (the
         # variant configuration as stated: 1M pairs), split into contiguous shards
         # over the ranks; timed per rank from the H2D copy of its shard's bases
@@ -668,7 +720,7 @@ def run_ours(args, world, rank, local):
             "dtype": "bf16" if args.mode == "bf16" else "f32", "data": "synthetic",
             "config": workload_config(args, world),
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "ism": ism,
-            "variant_pairs": var_run,
+            "variant_pairs": var_run, "other_configs": others,
             "clocks": clocks, "gpu_launches": launches_per_step * args.steps,
         }
         print(json.dumps(line), flush=True)
@@ -693,6 +745,8 @@ def main():
     ap.add_argument("--ref-sample", type=int, default=16)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-other-configs", action="store_true",
+                    help="forward workload: skip timing the multi-task and variant steps")
     args = ap.parse_args()
     if args.batch is None:
         args.batch = WORKLOADS[args.workload][1]
