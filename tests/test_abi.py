@@ -87,3 +87,14 @@ def test_calls_reject_null_pointers_without_touching_the_device():
                        None) == 1
     assert lib.chm_block_forward(1, 10, 128, 256, 1, 0, None, None, None, None, 0, None) == 1
     assert lib.chm_block_forward(1, 10, 128, 256, 1, 5, None, None, None, None, 0, None) == 1
+    assert lib.chm_ism_ex(ctypes.byref(d), None, 1, None, 0, 10, 8, None, None, None, None,
+                          0, None) == 1
+    # epilogues: null outputs/inputs, group sizes that do not cover the tracks
+    assert lib.chm_wrapper_epilogue(ctypes.byref(d), 1, None, None, None, None, None, None, 0,
+                                    None) == 1
+    bogus = ctypes.c_void_p(16)              # never dereferenced: rejected first
+    bad_groups = (ctypes.c_int32 * 1)(2)     # one track in the description, group of 2
+    assert lib.chm_wrapper_epilogue(ctypes.byref(d), 1, bogus, bogus, bad_groups, bogus, None,
+                                    None, 0, None) == 1
+    assert lib.chm_wrapper_epilogue(ctypes.byref(d), 1, bogus, bogus, None, None, bogus, None,
+                                    0, None) == 3   # the profile wrapper needs a workspace
