@@ -318,3 +318,51 @@ def test_forward_captures_in_cuda_graph(golden):
         g.replay()
         torch.cuda.synchronize()
         assert torch.equal(gp, ref_p) and torch.equal(gc, ref_c)
+
+
+@pytest.mark.parametrize("mode", ["fp32", "bf16"])
+def test_hidden_width_not_a_multiple_of_16(mode):
+    """Hidden widths the kernels pad (upstream tests/test_cheri.py:358-372,
+    611-629: H % 16 != 0 must still work): n_filters 24, expansion 1."""
+    torch.manual_seed(5)
+    m = cb.Cherimoya(n_filters=24, expansion=1, n_layers=4, trimming=80, compile=False,
+                     precision=mode).eval()
+    sd = {k: v.clone() for k, v in m.state_dict().items()}
+    X = O.one_hot(torch.randint(0, 4, (3, 500), generator=torch.Generator().manual_seed(6)))
+    with torch.no_grad():
+        rp, rc = O.forward(sd, m._init_kwargs(), X)
+    p, c = _run(m.to(DEV), X)
+    tol = FP32_TOL if mode == "fp32" else BF16_TOL
+    assert (p - rp).abs().max() <= tol and (c - rc).abs().max() <= tol
+
+
+def test_engine_matches_grad_path_on_cuda(golden):
+    """CUDA no_grad (the engine) against CUDA with gradients enabled (the
+    differentiable PyTorch ops) on the same model (upstream
+    tests/test_model.py:583-631: fp32 within 1e-4)."""
+    case = golden("model_default_L2114")
+    m = _model(case, "fp32")
+    X = O.one_hot(case["bases"]).to(DEV)
+    with torch.no_grad():
+        p0, c0 = m(X)
+    p1, c1 = m(X.clone().requires_grad_(True))
+    assert p1.requires_grad
+    assert (p0 - p1.detach()).abs().max().item() <= FP32_TOL
+    assert (c0 - c1.detach()).abs().max().item() <= FP32_TOL
+
+
+def test_block_hooks_bypassed_by_the_engine():
+    """Forward hooks on the blocks fire on the PyTorch path and not when the
+    engine runs the whole model (the documented upstream asymmetry,
+    tests/test_cheri.py:734-761)."""
+    m = cb.Cherimoya(n_filters=32, n_layers=2, compile=False, precision="fp32").eval().to(DEV)
+    calls = []
+    h = m.blocks[0].register_forward_hook(lambda mod, inp, out: calls.append(1))
+    X = torch.zeros(1, 4, 300, device=DEV)
+    X[:, 0] = 1.0
+    with torch.no_grad():
+        m(X)
+    assert calls == []
+    m(X.requires_grad_(True))
+    assert calls == [1]
+    h.remove()

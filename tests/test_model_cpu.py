@@ -152,3 +152,15 @@ def test_to_bases_and_shard_ranges():
             assert all(spans[i][1] == spans[i + 1][0] for i in range(world - 1))
             sizes = [hi - lo for lo, hi in spans]
             assert max(sizes) - min(sizes) <= 1
+
+
+def test_conv_norm_output_is_zero_mean_unit_variance():
+    """Per-example LayerNorm over the (L, C) plane (upstream tests/test_cheri.py:33-46):
+    mean 0 and biased variance var / (var + eps) ~ 1 for each example."""
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(3, 257, 24, generator=g) * 3.0 + 1.5
+    w = torch.randn(3, 24, generator=g)
+    y = cb.fused_dilated_conv_norm(x, w, 5)
+    flat = y.reshape(3, -1)
+    assert flat.mean(dim=1).abs().max().item() <= 1e-4
+    assert (flat.var(dim=1, unbiased=False) - 1.0).abs().max().item() <= 2e-3
