@@ -345,7 +345,13 @@ def test_engine_matches_grad_path_on_cuda(golden):
     X = O.one_hot(case["bases"]).to(DEV)
     with torch.no_grad():
         p0, c0 = m(X)
-    p1, c1 = m(X.clone().requires_grad_(True))
+    # the grad path's convolutions in plain fp32 (cuDNN would otherwise use TF32)
+    tf32 = torch.backends.cudnn.allow_tf32
+    torch.backends.cudnn.allow_tf32 = False
+    try:
+        p1, c1 = m(X.clone().requires_grad_(True))
+    finally:
+        torch.backends.cudnn.allow_tf32 = tf32
     assert p1.requires_grad
     assert (p0 - p1.detach()).abs().max().item() <= FP32_TOL
     assert (c0 - c1.detach()).abs().max().item() <= FP32_TOL
