@@ -2672,26 +2672,42 @@ __global__ void __launch_bounds__(hd3::kThreads, 1) head_fused_kernel(
   tc_fence_after();
   griddep_wait();                          // the previous kernel's outputs are visible
   const uint32_t tmem = *slot;
-  auto item_of = [&](int g, int& b, int& o, int& k) {
-    const int i = g / n_tiles;
-    k = g - i * n_tiles;
-    const int item = (int)blockIdx.x + i * (int)gridDim.x;
-    o = item / a.batch;
-    b = item - o * a.batch;
+  // Position of this CTA's sub-steps (item = blockIdx.x + i * gridDim.x,
+  // tile k of it, channel half sub), advanced one step at a time so that a
+  // step costs no integer division (only a change of item does).
+  struct Cursor {
+    int sub, k, item, o, b;
+  };
+  auto cur_init = [&](Cursor& c) {
+    c.sub = 0;
+    c.k = 0;
+    c.item = static_cast<int>(blockIdx.x);
+    c.o = c.item / a.batch;
+    c.b = c.item - c.o * a.batch;
+  };
+  auto cur_next = [&](Cursor& c, int subs) {
+    if (++c.sub < subs) return;
+    c.sub = 0;
+    if (++c.k < n_tiles) return;
+    c.k = 0;
+    c.item += static_cast<int>(gridDim.x);
+    c.o = c.item / a.batch;
+    c.b = c.item - c.o * a.batch;
   };
   bool ok = true;
   if (warp == hd3::kIssuerWarp) {
     // ------------------------------------------------------------ issuer
     // sub-step gs = (tile g, channel half gs % kSub) -> A buffer gs % kABufs
     const int total_sub = total * kSub;
-    auto load = [&](int gs) {
-      int b, o, k;
-      item_of(gs / kSub, b, o, k);
-      const int buf = gs % hd3::kABufs, x0 = 128 * (gs % kSub);
+    Cursor lc;                                          // next sub-step to load
+    cur_init(lc);
+    auto load = [&](int gs) {                           // gs = 0, 1, 2, ... in order
+      const int buf = gs % hd3::kABufs, x0 = 128 * lc.sub;
       mbar_expect_tx(&a_full[buf], 2 * kBox);
-      tma_load_3d(sA + buf * 2 * kBox, &tmap, x0, p0 + k * kTileRows, b, &a_full[buf]);
-      tma_load_3d(sA + buf * 2 * kBox + kBox, &tmap, x0 + 64, p0 + k * kTileRows, b,
+      tma_load_3d(sA + buf * 2 * kBox, &tmap, x0, p0 + lc.k * kTileRows, lc.b, &a_full[buf]);
+      tma_load_3d(sA + buf * 2 * kBox + kBox, &tmap, x0 + 64, p0 + lc.k * kTileRows, lc.b,
                   &a_full[buf]);
+      cur_next(lc, kSub);
     };
     if (lane == 0) {
       if (total_sub > 0) load(0);
@@ -2701,9 +2717,10 @@ __global__ void __launch_bounds__(hd3::kThreads, 1) head_fused_kernel(
     const uint32_t idesc = idesc_bf16(kTileRows, kNP);
     int cur_o = -1;
     uint32_t done_phase = 0;
-    for (int g = 0; g < total && ok; ++g) {
-      int b, o, k;
-      item_of(g, b, o, k);
+    Cursor ic;
+    cur_init(ic);
+    for (int g = 0; g < total && ok; ++g, cur_next(ic, 1)) {
+      const int o = ic.o;
       if (o != cur_o) {
         // operand F of output o, once the MMAs reading the previous one have
         // completed
@@ -2763,10 +2780,17 @@ __global__ void __launch_bounds__(hd3::kThreads, 1) head_fused_kernel(
     float cnt[hd3::kMaxGroups];
 #pragma unroll
     for (int gi = 0; gi < hd3::kMaxGroups; ++gi) cnt[gi] = 0.f;
-    for (int g = 0; g < total; ++g) {
-      int b, o, k;
-      item_of(g, b, o, k);
+    Cursor ec;
+    cur_init(ec);
+    int fb_o = -1;
+    float fbias = 0.f;                                  // bias of output fb_o
+    for (int g = 0; g < total; ++g, cur_next(ec, 1)) {
+      const int b = ec.b, o = ec.o, k = ec.k;
       const int zb = g & 1;
+      if (o != fb_o) {
+        fbias = __ldg(&a.fbias[o]);
+        fb_o = o;
+      }
       ok = mbar_wait(&z_full[zb], (g >> 1) & 1);
       if (!ok) break;
       tc_fence_after();
@@ -2816,7 +2840,7 @@ __global__ void __launch_bounds__(hd3::kThreads, 1) head_fused_kernel(
         const int j = j_lo + tid;
         if (j < j_hi)
           a.profile[((long long)b * a.n_out + o) * a.Lout + j] =
-              ((part[tid] + part[128 + tid]) + (part[256 + tid] + part[384 + tid])) + a.fbias[o];
+              ((part[tid] + part[128 + tid]) + (part[256 + tid] + part[384 + tid])) + fbias;
       }
       // ---- count head at the end of an item of output 0: fixed-order reduction
       if (o == 0 && k == n_tiles - 1) {
