@@ -491,14 +491,33 @@ __global__ void __launch_bounds__(sm2::kThreads, 1) stem_tc_kernel(
   const uint32_t bar_id = 1 + g;
   uint32_t it = 0;
   bool ok = true;
-  for (int tile = blockIdx.x * kG + g; tile < n_tiles; tile += gridDim.x * kG, ++it) {
+  // input columns gt and gt + 128 of the group's next tile, fetched while the
+  // current tile's MMAs and epilogue run
+  static_assert(kCols <= 256, "two staged columns per thread");
+  float pre[2][4];
+  auto fetch = [&](int tile_) {
+    const int b_ = tile_ / tpe;
+    const int l0_ = (tile_ - b_ * tpe) * kTileRows;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int p = l0_ + gt + 128 * h - kStemPad;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) pre[h][k] = 0.f;
+      if (tile_ < n_tiles && gt + 128 * h < kCols && p >= 0 && p < L)
+        stem_column<kIn>(in, L, b_, p, pre[h]);
+    }
+  };
+  const int tile_stride = gridDim.x * kG;
+  fetch(blockIdx.x * kG + g);
+  for (int tile = blockIdx.x * kG + g; tile < n_tiles; tile += tile_stride, ++it) {
     const int b = tile / tpe;
     const int l0 = (tile - b * tpe) * kTileRows;
     // ---- stage input columns l0 - 10 .. l0 + 137 (zero outside [0, L))
-    for (int i = gt; i < kCols; i += 128) {
-      const int p = l0 + i - kStemPad;
-      float col[4] = {0.f, 0.f, 0.f, 0.f};
-      if (p >= 0 && p < L) stem_column<kIn>(in, L, b, p, col);
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int i = gt + 128 * hh;
+      if (i >= kCols) continue;
+      const float(&col)[4] = pre[hh];
       const uint2 h = bf16x4_hi(col);
       cols[i] = h;
       if (kASplits > 1) {
@@ -549,6 +568,7 @@ __global__ void __launch_bounds__(sm2::kThreads, 1) stem_tc_kernel(
       }
       mma_commit(&bar[g]);
     }
+    fetch(tile + tile_stride);
     ok = mbar_wait(&bar[g], it & 1);
     if (!ok) {
       if (gt == 0) atomicExch(status, kStatusTimeout);
