@@ -2616,30 +2616,54 @@ __global__ void __launch_bounds__(hd::kThreads) head_kernel(HeadArgs a) {
 // count head rides in the same MMA: the five spare operand rows after the 75
 // taps hold the count Linear's weights (output 0 only), so Z[w, 75 + g] =
 // sum_c X[w, c] lw[g, c] and logcount[g] = lbias[g] + sum_w Z[w, 75 + g] / Lout
-// over the trimmed window. Diagonal sums of the profile are split over four
-// threads per output and combined in a fixed order (deterministic).
-// Warps 0-15 run the epilogue (Z -> ring -> diagonal sums -> profile); warp 16
-// issues the TMA loads and the MMAs, so Z of the next tile is computed while
-// the epilogue works on the current one (two TMEM buffers).
+// over the trimmed window.
+// Warp 17 streams the window tiles (three buffers, each refilled as soon as
+// the MMAs that read it have completed); warp 16 issues the MMAs. With F as
+// hi + lo (C = 128) the two halves are stacked into one N = 160 operand (rows
+// 80.. = lo), so each window tile is read once per K step and Z = Z_hi + Z_lo
+// is added in the epilogue. Z of tile g goes to TMEM buffer
+// g & 1 and is taken by epilogue group g & 1 (warps 0-7, 8-15), so the two
+// groups work on consecutive tiles at the same time. A group copies its Z tile
+// to its own shared-memory buffer and sums the tile's part of every diagonal
+// it touches: outputs j = 128 k - 74 + s, s < 202, each over its taps t with
+// row j + t inside the tile, in four 20-tap items combined by shuffles in a
+// fixed order. Outputs 128 k .. 128 k + 53 are complete in the tile. The 74
+// outputs that continue into the next tile (s >= 128) go, with the running
+// sums of the count columns, to the group's carry buffer, and the next tile's
+// group adds its own part to them. The carry is handed over tile by tile
+// (c_full / c_empty), so every output and count is summed in tile order
+// (deterministic).
 namespace hd3 {
-constexpr int kEpiThreads = 512;
-constexpr int kIssuerWarp = kEpiThreads / 32;
-constexpr int kTapParts = kEpiThreads / 128;             // threads per output's diagonal
-static_assert(kTapParts == 4, "the profile store sums four tap parts");
-constexpr int kThreads = kEpiThreads + 32;
+constexpr int kGroupWarps = 8;                           // epilogue warps per group
+constexpr int kGroupThreads = kGroupWarps * 32;
+constexpr int kEpiThreads = 2 * kGroupThreads;           // two groups, alternate tiles
+constexpr int kIssuerWarp = kEpiThreads / 32;           // MMAs
+constexpr int kTmaWarp = kIssuerWarp + 1;                // window-tile loads
+constexpr int kThreads = kEpiThreads + 64;
 constexpr int kABufs = 3;
 constexpr int kMaxGroups = hd::kNP - kHeadTaps;          // 5 spare operand rows
+constexpr int kZCols = 2 * hd::kNP;                      // TMEM columns per Z buffer
+constexpr int kCarry = kHeadTaps - 1;                    // outputs that straddle two tiles
+constexpr int kSpan = kTileRows + kCarry;                // outputs a tile contributes to
+constexpr int kPartTaps = 20;                            // taps per partial-sum item
+constexpr int kParts = 4;                                // items per output (75 taps)
+static_assert(kParts * kPartTaps >= kHeadTaps && (kParts - 1) * kPartTaps < kHeadTaps,
+              "tap parts");
+constexpr int kPasses = (kSpan * kParts + kGroupThreads - 1) / kGroupThreads;
 constexpr uint32_t kBox = 128 * 128;                     // 16 KB: 64 channels x 128 rows
 constexpr uint32_t kB = 0;                               // F hi | lo: 2 x 80 x 128 bf16
 constexpr uint32_t kA = 40960;                           // kABufs x 2 boxes
-constexpr uint32_t kRingOff = kA + kABufs * 2 * kBox;
-constexpr uint32_t kPart = kRingOff + hd::kRing * hd::kZStride * 4;
-constexpr uint32_t kRed = kPart + kTapParts * 128 * 4;
-constexpr uint32_t kBars = kRed + 8 * kMaxGroups * 4 + 32;
-constexpr int kNumBars = 2 * kABufs + 5;  // a_full[3] z_full[2] z_free[2] mma_done a_free[3]
+constexpr uint32_t kZsBytes = kTileRows * hd::kZStride * 4;
+constexpr uint32_t kZs = kA + kABufs * 2 * kBox;         // [group][128 rows][kZStride] fp32
+constexpr uint32_t kCarryOff = kZs + 2 * kZsBytes;       // [group][80]: tail partials, counts
+constexpr uint32_t kRed = kCarryOff + 2 * 80 * 4;        // [group][4 warps][kMaxGroups]
+constexpr uint32_t kBars = kRed + 2 * 4 * kMaxGroups * 4;
+// a_full[3] z_full[2] z_free[2] mma_done a_free[3] c_full[2] c_empty[2] f_full
+constexpr int kNumBars = 2 * kABufs + 10;
 constexpr uint32_t kSlot = kBars + kNumBars * 8;
 constexpr uint32_t kAlloc = kSlot + 16 + 1024;
 static_assert(kA % 1024 == 0 && 2 * hd::kNP * 128 * 2 <= kA, "operand layout");
+static_assert(kBars % 8 == 0 && kCarry + kMaxGroups <= 80, "carry layout");
 static_assert(kAlloc <= 232448, "shared memory per block");
 }  // namespace hd3
 
@@ -2661,9 +2685,6 @@ __global__ void __launch_bounds__(hd3::kThreads, 1) head_fused_kernel(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sB = smem + hd3::kB;
   uint8_t* sA = smem + hd3::kA;
-  float* ring = reinterpret_cast<float*>(smem + hd3::kRingOff);
-  float* part = reinterpret_cast<float*>(smem + hd3::kPart);      // [2][128]
-  float* red = reinterpret_cast<float*>(smem + hd3::kRed);        // [8 warps][groups]
   uint64_t* a_full = reinterpret_cast<uint64_t*>(smem + hd3::kBars);   // [kABufs]
   uint64_t* z_full = a_full + hd3::kABufs;                              // [2]
   uint32_t* slot = reinterpret_cast<uint32_t*>(smem + hd3::kSlot);
@@ -2680,11 +2701,17 @@ __global__ void __launch_bounds__(hd3::kThreads, 1) head_fused_kernel(
   uint64_t* z_free = z_full + 2;                                        // [2]
   uint64_t* mma_done = z_free + 2;
   uint64_t* a_free = mma_done + 1;                                      // [kABufs]
-  if (warp == 0) tmem_alloc(slot, 256);
+  uint64_t* c_full = a_free + hd3::kABufs;                              // [2]
+  uint64_t* c_empty = c_full + 2;                                       // [2]
+  uint64_t* f_full = c_empty + 2;
+  if (warp == 0) tmem_alloc(slot, 512);
   if (tid == 0) {
     for (int i = 0; i < hd3::kNumBars; ++i) mbar_init(&a_full[i], 1);
-    mbar_init(&z_free[0], hd3::kEpiThreads / 32);
-    mbar_init(&z_free[1], hd3::kEpiThreads / 32);
+    for (int e = 0; e < 2; ++e) {                       // one arrive per group warp
+      mbar_init(&z_free[e], hd3::kGroupWarps);
+      mbar_init(&c_full[e], hd3::kGroupWarps);
+      mbar_init(&c_empty[e], hd3::kGroupWarps);
+    }
     mbar_init_fence();
   }
   tc_fence_before();
@@ -2715,76 +2742,81 @@ __global__ void __launch_bounds__(hd3::kThreads, 1) head_fused_kernel(
     c.b = c.item - c.o * a.batch;
   };
   bool ok = true;
-  if (warp == hd3::kIssuerWarp) {
-    // ------------------------------------------------------------ issuer
-    // sub-step gs = (tile g, channel half gs % kSub) -> A buffer gs % kABufs
-    const int total_sub = total * kSub;
-    Cursor lc;                                          // next sub-step to load
-    cur_init(lc);
-    auto load = [&](int gs) {                           // gs = 0, 1, 2, ... in order
-      const int buf = gs % hd3::kABufs, x0 = 128 * lc.sub;
-      mbar_expect_tx(&a_full[buf], 2 * kBox);
-      tma_load_3d(sA + buf * 2 * kBox, &tmap, x0, p0 + lc.k * kTileRows, lc.b, &a_full[buf]);
-      tma_load_3d(sA + buf * 2 * kBox + kBox, &tmap, x0 + 64, p0 + lc.k * kTileRows, lc.b,
-                  &a_full[buf]);
-      cur_next(lc, kSub);
-    };
+  if (warp == hd3::kTmaWarp) {
+    // ------------------------------------------------------------ window tiles
+    // sub-step gs = (tile g, channel half gs % kSub) -> A buffer gs % kABufs,
+    // refilled once the MMAs of sub-step gs - kABufs have completed
     if (lane == 0) {
-      if (total_sub > 0) load(0);
-      if (total_sub > 1) load(1);
+      const int total_sub = total * kSub;
+      Cursor lc;
+      cur_init(lc);
+      for (int gs = 0; gs < total_sub && ok; ++gs, cur_next(lc, kSub)) {
+        const int buf = gs % hd3::kABufs;
+        if (gs >= hd3::kABufs)
+          ok = mbar_wait(&a_free[buf], ((gs - hd3::kABufs) / hd3::kABufs) & 1);
+        if (!ok) break;
+        const int x0 = 128 * lc.sub;
+        mbar_expect_tx(&a_full[buf], 2 * kBox);
+        tma_load_3d(sA + buf * 2 * kBox, &tmap, x0, p0 + lc.k * kTileRows, lc.b, &a_full[buf]);
+        tma_load_3d(sA + buf * 2 * kBox + kBox, &tmap, x0 + 64, p0 + lc.k * kTileRows, lc.b,
+                    &a_full[buf]);
+      }
     }
+    __syncwarp();
+  } else if (warp == hd3::kIssuerWarp) {
+    // ------------------------------------------------------------ MMAs
     const uint32_t sA_addr = smem_u32(sA), sB_addr = smem_u32(sB);
-    const uint32_t idesc = idesc_bf16(kTileRows, kNP);
+    constexpr uint32_t kSlabB = kTerms * kNP * 128;      // bytes per 64-channel slab of F
+    const uint32_t idesc = idesc_bf16(kTileRows, kTerms * kNP);
     int cur_o = -1;
-    uint32_t done_phase = 0;
+    uint32_t done_phase = 0, f_phase = 0;
     Cursor ic;
     cur_init(ic);
     for (int g = 0; g < total && ok; ++g, cur_next(ic, 1)) {
       const int o = ic.o;
       if (o != cur_o) {
-        // operand F of output o, once the MMAs reading the previous one have
-        // completed
-        if (g > 0) {
-          if (lane == 0) {
+        // operand F of output o by bulk copies, once the MMAs reading the
+        // previous one have completed: per 64-channel slab, the hi rows then
+        // (C = 128) the lo rows
+        if (lane == 0) {
+          if (g > 0) {
             mma_commit(mma_done);
             ok = mbar_wait(mma_done, done_phase & 1);
           }
-          ++done_phase;
-          ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-          if (!ok) break;
+          if (ok) {
+            constexpr uint32_t kSlabBytes = kNP * 128;   // one slab of one term
+            constexpr uint32_t kTermBytes = kSlabBytes * (CPH / 64);
+            const uint8_t* src = a.fb + (size_t)o * 2 * kNP * CPH * 2;
+            mbar_expect_tx(f_full, kTerms * kTermBytes);
+            for (int term = 0; term < kTerms; ++term)
+              for (int slab = 0; slab < CPH / 64; ++slab)
+                bulk_load(sB + (slab * kTerms + term) * kSlabBytes,
+                          src + term * kTermBytes + slab * kSlabBytes, kSlabBytes, f_full);
+            ok = mbar_wait(f_full, f_phase & 1);
+          }
         }
-        const uint4* src = reinterpret_cast<const uint4*>(a.fb + (size_t)o * 2 * kNP * CPH * 2);
-        uint4* dst = reinterpret_cast<uint4*>(sB);
-        for (int i = lane; i < kTerms * kNP * CPH * 2 / 16; i += 32) dst[i] = src[i];
-        fence_async_smem();
-        __syncwarp();
+        if (g > 0) ++done_phase;
+        ++f_phase;
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (!ok) break;
         cur_o = o;
       }
       if (lane == 0) {
         const int zb = g & 1;
         for (int half = 0; half < kSub && ok; ++half) {
           const int gs = g * kSub + half, buf = gs % hd3::kABufs;
-          // A[(gs + 2) % 3] was last read by the MMAs of sub-step gs - 1
-          if (gs + 2 < total_sub) {
-            if (gs >= 1)
-              ok = mbar_wait(&a_free[(gs - 1) % hd3::kABufs], ((gs - 1) / hd3::kABufs) & 1);
-            if (ok) load(gs + 2);
-          }
-          ok = ok && mbar_wait(&a_full[buf], (gs / hd3::kABufs) & 1);
+          ok = mbar_wait(&a_full[buf], (gs / hd3::kABufs) & 1);
           // TMEM buffer zb was released by the epilogue of tile g - 2
           if (half == 0) ok = ok && mbar_wait(&z_free[zb], ((g >> 1) & 1) ^ 1);
           if (!ok) break;
           tc_fence_after();
-          for (int term = 0; term < kTerms; ++term) {    // F hi (, F lo)
 #pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
-              const uint64_t da = desc_sw128(sA_addr + buf * 2 * kBox + (kk >> 2) * kBox +
-                                             (kk & 3) * 32);
-              const uint64_t db = desc_sw128(sB_addr + term * (kNP * CPH * 2) +
-                                             (2 * half + (kk >> 2)) * (kNP * 128) + (kk & 3) * 32);
-              mma_bf16(tmem + zb * 128, da, db, idesc,
-                       (half > 0 || term > 0 || kk > 0) ? 1u : 0u);
-            }
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t da = desc_sw128(sA_addr + buf * 2 * kBox + (kk >> 2) * kBox +
+                                           (kk & 3) * 32);
+            const uint64_t db = desc_sw128(sB_addr + (2 * half + (kk >> 2)) * kSlabB +
+                                           (kk & 3) * 32);
+            mma_bf16(tmem + zb * hd3::kZCols, da, db, idesc, (half > 0 || kk > 0) ? 1u : 0u);
           }
           mma_commit(&a_free[buf]);
           if (half == kSub - 1) mma_commit(&z_full[zb]);
@@ -2794,94 +2826,155 @@ __global__ void __launch_bounds__(hd3::kThreads, 1) head_fused_kernel(
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int rq = warp & 3;                            // TMEM lane quarter
+    using hd3::kCarry;
+    using hd3::kMaxGroups;
+    const int e = warp / hd3::kGroupWarps;              // group: tiles g with g & 1 == e
+    const int gw = warp % hd3::kGroupWarps;
+    const int rq = gw & 3;                              // TMEM lane quarter (warp % 4)
+    const int ch = gw >> 2;                             // column half: [0, 48) / [48, 80)
+    const int gt = tid % hd3::kGroupThreads;
     const uint32_t lane_sel = static_cast<uint32_t>(rq * 32) << 16;
-    const int w = rq * 32 + lane;                       // tile row of this thread (Z pass)
-    float cnt[hd3::kMaxGroups];
+    const uint32_t zcol = tmem + e * hd3::kZCols;
+    // Z column c = hi column c (+ lo column kNP + c); count columns likewise
+    auto zload16 = [&](int c0, uint32_t (&r)[16]) {
+      tmem_ld16(zcol + lane_sel + c0, r);
+      if (kTerms == 2) {
+        uint32_t q2[16];
+        tmem_ld16(zcol + lane_sel + kNP + c0, q2);
 #pragma unroll
-    for (int gi = 0; gi < hd3::kMaxGroups; ++gi) cnt[gi] = 0.f;
+        for (int q = 0; q < 16; ++q)
+          r[q] = __float_as_uint(__uint_as_float(r[q]) + __uint_as_float(q2[q]));
+      }
+    };
+    const int w = rq * 32 + lane;                       // tile row = TMEM lane
+    float* Zs = reinterpret_cast<float*>(smem + hd3::kZs + e * hd3::kZsBytes);
+    float* carry_mine = reinterpret_cast<float*>(smem + hd3::kCarryOff) + e * 80;
+    const float* carry_prev = reinterpret_cast<const float*>(smem + hd3::kCarryOff) + (e ^ 1) * 80;
+    float* red = reinterpret_cast<float*>(smem + hd3::kRed) + e * 4 * kMaxGroups;
     Cursor ec;
     cur_init(ec);
+    if (e == 1) cur_next(ec, 1);
     int fb_o = -1;
     float fbias = 0.f;                                  // bias of output fb_o
-    for (int g = 0; g < total; ++g, cur_next(ec, 1)) {
+    for (int g = e, n = 0; g < total; g += 2, ++n, cur_next(ec, 1), cur_next(ec, 1)) {
       const int b = ec.b, o = ec.o, k = ec.k;
-      const int zb = g & 1;
       if (o != fb_o) {
         fbias = __ldg(&a.fbias[o]);
         fb_o = o;
       }
-      ok = mbar_wait(&z_full[zb], (g >> 1) & 1);
+      const bool counts = (o == 0);
+      ok = mbar_wait(&z_full[e], n & 1);
       if (!ok) break;
       tc_fence_after();
-      // ---- Z tile -> ring rows (128 k + w) mod kRing; column group cg of the
-      // warp: [0, 32), [32, 64), [64, 80) (taps 64..74 and the count columns);
-      // group 3 has no columns
-      const int cg = warp >> 2;
+      // ---- Z tile -> Zs (rows w, taps); count columns summed per warp
       {
-        float* zrow = ring + ((k * kTileRows + w) % kRing) * kZStride;
-        if (cg < 2) {
-          uint32_t r[32];
-          tmem_ld32(tmem + zb * 128 + lane_sel + cg * 32, r);
+        float* zrow = Zs + w * kZStride;
+        if (ch == 0) {
+#pragma unroll 1
+          for (int c0 = 0; c0 < 48; c0 += 16) {
+            uint32_t r[16];
+            zload16(c0, r);
 #pragma unroll
-          for (int q = 0; q < 32; ++q) zrow[cg * 32 + q] = __uint_as_float(r[q]);
-        } else if (cg == 2) {
+            for (int q = 0; q < 16; ++q) zrow[c0 + q] = __uint_as_float(r[q]);
+          }
+          tc_fence_before();
+          mbar_arrive_warp(&z_free[e]);                 // TMEM buffer e is free again
+        } else {
           uint32_t r[16];
-          tmem_ld16(tmem + zb * 128 + lane_sel + 64, r);   // columns 64..79
+          zload16(48, r);
 #pragma unroll
-          for (int q = 0; q < kHeadTaps - 64; ++q) zrow[64 + q] = __uint_as_float(r[q]);
-          const int wr = k * kTileRows + w;                // window row
-          if (o == 0 && wr >= kHeadPad && wr < kHeadPad + a.Lout) {
+          for (int q = 0; q < 16; ++q) zrow[48 + q] = __uint_as_float(r[q]);
+          uint32_t r2[16];
+          zload16(64, r2);                              // taps 64..74, count columns
 #pragma unroll
-            for (int gi = 0; gi < hd3::kMaxGroups; ++gi)
-              cnt[gi] += __uint_as_float(r[kHeadTaps - 64 + gi]);
+          for (int q = 0; q < kHeadTaps - 64; ++q) zrow[64 + q] = __uint_as_float(r2[q]);
+          tc_fence_before();
+          mbar_arrive_warp(&z_free[e]);
+          if (counts) {
+            const int wr = k * kTileRows + w;           // window row
+            const bool in = wr >= kHeadPad && wr < kHeadPad + a.Lout;
+#pragma unroll
+            for (int gi = 0; gi < kMaxGroups; ++gi) {
+              float v = in ? __uint_as_float(r2[kHeadTaps - 64 + gi]) : 0.f;
+#pragma unroll
+              for (int sh = 16; sh > 0; sh >>= 1) v += __shfl_xor_sync(0xffffffffu, v, sh);
+              if (lane == 0) red[rq * kMaxGroups + gi] = v;
+            }
           }
         }
       }
-      tc_fence_before();
-      mbar_arrive_warp(&z_free[zb]);                      // TMEM buffer zb is free again
-      named_sync(1, hd3::kEpiThreads);
-      // ---- diagonal sums: output j = sum_t ring[(j + t) mod kRing][t], in
-      // kTapParts tap ranges
-      const int j_lo = (k == 0) ? 0 : k * kTileRows - (kHeadTaps - 1);
-      const int j_hi = (k == n_tiles - 1) ? a.Lout
-                                          : min(a.Lout, k * kTileRows + kTileRows - (kHeadTaps - 1));
-      {
-        const int jj = tid & 127, tp = tid >> 7;
-        const int j = j_lo + jj;
-        if (j < j_hi) {
-          const int t0 = (tp * kHeadTaps) / hd3::kTapParts;
-          const int t1 = ((tp + 1) * kHeadTaps) / hd3::kTapParts;
-          part[tp * 128 + jj] = ring_diag_sum(ring, (j + t0) % kRing, t0, t1 - t0);
-        }
-      }
-      named_sync(1, hd3::kEpiThreads);
-      if (tid < 128) {
-        const int j = j_lo + tid;
-        if (j < j_hi)
-          a.profile[((long long)b * a.n_out + o) * a.Lout + j] =
-              ((part[tid] + part[128 + tid]) + (part[256 + tid] + part[384 + tid])) + fbias;
-      }
-      // ---- count head at the end of an item of output 0: fixed-order reduction
-      if (o == 0 && k == n_tiles - 1) {
-        if (cg == 2) {
+      named_sync(1 + e, hd3::kGroupThreads);
+      // ---- this tile's part of the diagonals: item = 4 s + p covers taps
+      // [20 p, 20 p + 20) of output s whose rows s - 74 + t lie in [0, 128)
+      // (the four passes' chains run interleaved, each summed in tap order)
+      float pv[hd3::kPasses];
+      int pidx[hd3::kPasses], plen[hd3::kPasses];
 #pragma unroll
-          for (int gi = 0; gi < hd3::kMaxGroups; ++gi) {
-            float v = cnt[gi];
+      for (int pass = 0; pass < hd3::kPasses; ++pass) {
+        const int item = pass * hd3::kGroupThreads + gt;
+        const int so = item >> 2, pp = item & 3;
+        const int t_lo = max(pp * hd3::kPartTaps, kCarry - so);
+        const int t_hi = min(min(pp * hd3::kPartTaps + hd3::kPartTaps, kHeadTaps), hd3::kSpan - so);
+        plen[pass] = (so < hd3::kSpan) ? max(0, t_hi - t_lo) : 0;
+        pidx[pass] = (so - kCarry + t_lo) * kZStride + t_lo;
+        pv[pass] = 0.f;
+      }
+#pragma unroll 4
+      for (int u = 0; u < hd3::kPartTaps; ++u) {
 #pragma unroll
-            for (int sh = 16; sh > 0; sh >>= 1) v += __shfl_xor_sync(0xffffffffu, v, sh);
-            if (lane == 0) red[(warp - 8) * hd3::kMaxGroups + gi] = v;
-            cnt[gi] = 0.f;
+        for (int pass = 0; pass < hd3::kPasses; ++pass)
+          if (u < plen[pass]) pv[pass] += Zs[pidx[pass] + u * (kZStride + 1)];
+      }
+#pragma unroll
+      for (int pass = 0; pass < hd3::kPasses; ++pass) {
+        float v = pv[pass];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        pv[pass] = v;                                   // (p0 + p1) + (p2 + p3)
+      }
+      float tile_cnt = 0.f;                             // threads gt < kMaxGroups
+      if (counts && gt < kMaxGroups)
+        tile_cnt = ((red[gt] + red[kMaxGroups + gt]) + red[2 * kMaxGroups + gt]) +
+                   red[3 * kMaxGroups + gt];
+      // ---- outputs: s < 74 complete with the previous tile's carry, 74 <= s
+      // < 128 are complete here
+      if (g > 0) {
+        ok = mbar_wait(&c_full[e ^ 1], ((g - 1) >> 1) & 1);
+        if (!ok) break;
+      }
+      float* prof = a.profile + ((long long)b * a.n_out + o) * a.Lout;
+#pragma unroll
+      for (int pass = 0; pass < 2; ++pass) {
+        const int so = (pass * hd3::kGroupThreads + gt) >> 2;
+        const int j = k * kTileRows - kCarry + so;
+        if ((gt & 3) == 0 && j < a.Lout) {
+          if (so < kCarry) {
+            if (k > 0) prof[j] = (carry_prev[so] + pv[pass]) + fbias;
+          } else {
+            prof[j] = pv[pass] + fbias;
           }
         }
-        named_sync(1, hd3::kEpiThreads);
-        if (tid < a.n_groups) {
-          const float s4 = ((red[tid] + red[hd3::kMaxGroups + tid]) +
-                            red[2 * hd3::kMaxGroups + tid]) + red[3 * hd3::kMaxGroups + tid];
-          a.logcounts[(long long)b * a.n_groups + tid] =
-              a.lbias[tid] + s4 / static_cast<float>(a.Lout);
-        }
       }
+      float run = 0.f;                                  // count sums through tile k
+      if (counts && gt < kMaxGroups) {
+        run = (k == 0) ? tile_cnt : carry_prev[kCarry + gt] + tile_cnt;
+        if (k == n_tiles - 1 && gt < a.n_groups)
+          a.logcounts[(long long)b * a.n_groups + gt] = a.lbias[gt] + run / static_cast<float>(a.Lout);
+      }
+      if (g > 0) mbar_arrive_warp(&c_empty[e ^ 1]);     // done with the previous carry
+      // ---- carry for the next tile: outputs s >= 128, running count sums
+      if (n > 0) {
+        ok = mbar_wait(&c_empty[e], (n - 1) & 1);
+        if (!ok) break;
+      }
+#pragma unroll
+      for (int pass = 2; pass < hd3::kPasses; ++pass) {
+        const int so = (pass * hd3::kGroupThreads + gt) >> 2;
+        if ((gt & 3) == 0 && so < hd3::kSpan) carry_mine[so - kTileRows] = pv[pass];
+      }
+      if (gt < kMaxGroups) carry_mine[kCarry + gt] = run;
+      mbar_arrive_warp(&c_full[e]);
+      named_sync(1 + e, hd3::kGroupThreads);            // Zs and red are free again
     }
   }
   if (!ok) atomicExch(a.status, kStatusTimeout);
@@ -2889,7 +2982,7 @@ __global__ void __launch_bounds__(hd3::kThreads, 1) head_fused_kernel(
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 
