@@ -421,7 +421,7 @@ __host__ __device__ constexpr uint32_t cols_stride(int a_splits) {
 }
 __host__ __device__ constexpr uint32_t smem_bytes(int a_splits, int out_bytes = 2) {
   return cols_off(a_splits, out_bytes) + groups_for(out_bytes) * cols_stride(a_splits) +
-         128 * 4 + 8 * groups_for(out_bytes) + 16 + 1024;
+         128 * 4 + 8 * (groups_for(out_bytes) + 1) + 16 + 1024;
 }
 static_assert(smem_bytes(1) <= 232448, "shared memory per block");
 static_assert(smem_bytes(2, 4) <= 232448, "shared memory per block (fp32 output)");
@@ -458,26 +458,25 @@ __global__ void __launch_bounds__(sm2::kThreads, 1) stem_tc_kernel(
   float* sbias = reinterpret_cast<float*>(smem + cols_off(kASplits, sizeof(out_t)) +
                                           kG * cols_stride(kASplits));
   uint64_t* bar = reinterpret_cast<uint64_t*>(sbias + 128);    // [kG]
-  uint32_t* slot = reinterpret_cast<uint32_t*>(bar + kG);
+  uint64_t* wbar = bar + kG;                                     // W pieces arrived
+  uint32_t* slot = reinterpret_cast<uint32_t*>(wbar + 1);
   if (warp == 0) tmem_alloc(slot, 128 * kG);
   if (tid == 0) {
     for (int i = 0; i < kG; ++i) mbar_init(&bar[i], 1);
+    mbar_init(wbar, 1);
     mbar_init_fence();
-  }
-  {
     // rows [c_off, c_off + 128) of the hi and lo halves, both K boxes: four
-    // 16 KB pieces [split][box]
-    uint4* dst = reinterpret_cast<uint4*>(sB);
-    constexpr int kPiece = 128 * 128 / 16;
-    for (int i = tid; i < static_cast<int>(kW / 16); i += blockDim.x) {
-      const int piece = i / kPiece, e = i - piece * kPiece;
+    // 16 KB pieces [split][box], by bulk copies (packed weights only)
+    constexpr uint32_t kPiece = 128 * 128;
+    mbar_expect_tx(wbar, kW);
+    for (int piece = 0; piece < static_cast<int>(kW / kPiece); ++piece) {
       const int sp = piece >> 1, kb = piece & 1;
       const size_t off = static_cast<size_t>(sp) * CP * sm::kK * 2 +
                          static_cast<size_t>(kb) * CP * 128 + static_cast<size_t>(c_off) * 128;
-      dst[i] = reinterpret_cast<const uint4*>(wpk + off)[e];
+      bulk_load(sB + piece * kPiece, wpk + off, kPiece, wbar);
     }
-    if (tid < 128) sbias[tid] = c_off + tid < C ? bias[c_off + tid] : 0.f;
   }
+  if (tid < 128) sbias[tid] = c_off + tid < C ? bias[c_off + tid] : 0.f;
   fence_async_smem();
   tc_fence_before();
   __syncthreads();
@@ -509,7 +508,11 @@ __global__ void __launch_bounds__(sm2::kThreads, 1) stem_tc_kernel(
   };
   const int tile_stride = gridDim.x * kG;
   fetch(blockIdx.x * kG + g);
-  for (int tile = blockIdx.x * kG + g; tile < n_tiles; tile += tile_stride, ++it) {
+  // every thread (so every CTA, with or without tiles) waits for the weight
+  // pieces once, while its first input columns are in flight
+  ok = mbar_wait(wbar, 0);
+  if (!ok && tid == 0) atomicExch(status, kStatusTimeout);
+  for (int tile = blockIdx.x * kG + g; ok && tile < n_tiles; tile += tile_stride, ++it) {
     const int b = tile / tpe;
     const int l0 = (tile - b * tpe) * kTileRows;
     // ---- stage input columns l0 - 10 .. l0 + 137 (zero outside [0, L))
@@ -1648,7 +1651,7 @@ constexpr uint32_t kStg = kW2 + kC * kH * 2;                    // staging ring
 constexpr int kMaxSlots = 5;
 enum Bar : int { STG_FULL0 = 0, STG_EMPTY0 = kMaxSlots, A1_FULL0 = 2 * kMaxSlots, A1_FULL1,
                  A1_EMPTY0, A1_EMPTY1, D1A_FULL, D1B_FULL, A2A_FULL, A2B_FULL, D2_FULL,
-                 RES_FULL, RES_DONE, D2_EMPTY, kNumBars };
+                 RES_FULL, RES_DONE, D2_EMPTY, W_FULL, kNumBars };
 // Staging ring. Split mode (any dilation): a box step covers kBoxBytes of
 // channels and a slot holds its three 128-row blocks (rows - d, rows,
 // rows + d), 64-byte rows with the 64-byte swizzle. Wide mode (bf16, d <= 64):
@@ -1730,14 +1733,16 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
     }
     *abort_flag = 0;
     mbar_init_fence();
+    // W1 and W2 (packed weights only: allowed before griddep_wait) by bulk
+    // copies; the MMA warp waits for them
+    constexpr uint32_t kWBytes = kH * kC * 2, kPiece = 16384;
+    mbar_expect_tx(&bars[W_FULL], 2 * kWBytes);
+    for (uint32_t off = 0; off < kWBytes; off += kPiece) {
+      bulk_load(smem + kW1 + off, a.w1 + off, kPiece, &bars[W_FULL]);
+      bulk_load(smem + kW2 + off, a.w2 + off, kPiece, &bars[W_FULL]);
+    }
   }
   {
-    const uint4* g1 = reinterpret_cast<const uint4*>(a.w1);
-    const uint4* g2 = reinterpret_cast<const uint4*>(a.w2);
-    uint4* s1 = reinterpret_cast<uint4*>(smem + kW1);
-    uint4* s2 = reinterpret_cast<uint4*>(smem + kW2);
-    for (int i = tid; i < kH * kC * 2 / 16; i += blockDim.x) s1[i] = g1[i];
-    for (int i = tid; i < kC * kH * 2 / 16; i += blockDim.x) s2[i] = g2[i];
     if constexpr (sizeof(act_t) == 2) {
       // bf16 activations: conv weights as bf16x2 channel pairs [tap][pair]
       uint32_t* cw = reinterpret_cast<uint32_t*>(smem + kConvW);
@@ -2101,7 +2106,11 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0 && n_my > 0) {
+    // (the weights' bulk copies are waited for even without tiles, so no
+    // copy into this CTA's shared memory outlives it)
+    bool w_ok = true;
+    if (lane == 0) w_ok = mbar_wait_abortable(&bars[W_FULL], 0, abort_flag);
+    if (lane == 0 && n_my > 0 && w_ok) {
       const uint32_t sW1 = smem_u32(smem + kW1), sW2 = smem_u32(smem + kW2);
       constexpr uint32_t kIdesc = idesc_bf16(kTileRows, 128);
       auto g1 = [&](int hh, int buf) {  // D1x = A1(tmem) * W1[hh*128 : hh*128+128]^T, K = 128
