@@ -73,6 +73,35 @@ def test_multitask_c128_9layer_against_oracle(mode):
     _check(mode, p.cpu(), c.cpu(), rp, rc, "multitask")
 
 
+@pytest.mark.parametrize("N,Lseq,T,groups,C", [
+    (1, 129, 60, None, 128),       # 83-row window: one tile
+    (3, 300, 53, None, 128),       # three tiles
+    (200, 300, 53, None, 128),     # more items than CTAs: item boundaries inside a CTA
+    (160, 400, 100, [2, 1], 128),  # three tracks, two count heads, 480 items
+    (2, 2114, 0, None, 128),       # 2188-row window: eighteen tiles
+    (4, 1000, 37, None, 128),      # eight tiles
+    (150, 300, 53, None, 256),     # n_filters 256: two channel halves per tile
+])
+def test_fused_head_window_lengths_bf16(N, Lseq, T, groups, C):
+    """The bf16 fused head sums each profile diagonal per tile and carries the
+    74 outputs that straddle two tiles to the next tile's epilogue group; the
+    count columns travel in the same carry. Window lengths of 1 to 18 tiles,
+    odd and even tile counts, several items per CTA and several tracks."""
+    torch.manual_seed(5)
+    kw = {} if groups is None else {"signal_groups": groups}
+    m = cb.Cherimoya(n_filters=C, n_layers=2, trimming=T, compile=False, precision="bf16",
+                     **kw).eval()
+    sd = {k: v.clone() for k, v in m.state_dict().items()}
+    g = torch.Generator().manual_seed(6)
+    X = O.one_hot(torch.randint(0, 4, (N, Lseq), generator=g))
+    with torch.no_grad():
+        rp, rc = O.forward(sd, m._init_kwargs(), X)
+        p, c = m.to(DEV)(X.to(DEV))
+    torch.cuda.synchronize()
+    assert p.shape == rp.shape and c.shape == rc.shape
+    _check("bf16", p.cpu(), c.cpu(), rp, rc, "head L=%d T=%d N=%d" % (Lseq, T, N))
+
+
 def _golden_model(case, mode):
     m = cb.Cherimoya(**case["config"], compile=False, precision=mode)
     m.load_state_dict(case["state_dict"])
