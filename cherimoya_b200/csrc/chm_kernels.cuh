@@ -2664,15 +2664,16 @@ constexpr uint32_t kB = 0;                               // F hi | lo: 2 x 80 x 
 constexpr uint32_t kA = 40960;                           // kABufs x 2 boxes
 constexpr uint32_t kZsBytes = kTileRows * hd::kZStride * 4;
 constexpr uint32_t kZs = kA + kABufs * 2 * kBox;         // [group][128 rows][kZStride] fp32
-constexpr uint32_t kCarryOff = kZs + 2 * kZsBytes;       // [group][80]: tail partials, counts
-constexpr uint32_t kRed = kCarryOff + 2 * 80 * 4;        // [group][4 warps][kMaxGroups]
+constexpr int kCarryStride = 80;                         // tail partials, then count sums
+constexpr uint32_t kCarryOff = kZs + 2 * kZsBytes;       // [group][kCarryStride] fp32
+constexpr uint32_t kRed = kCarryOff + 2 * kCarryStride * 4;   // [group][4 warps][kMaxGroups]
 constexpr uint32_t kBars = kRed + 2 * 4 * kMaxGroups * 4;
 // a_full[3] z_full[2] z_free[2] mma_done a_free[3] c_full[2] c_empty[2] f_full
 constexpr int kNumBars = 2 * kABufs + 10;
 constexpr uint32_t kSlot = kBars + kNumBars * 8;
 constexpr uint32_t kAlloc = kSlot + 16 + 1024;
 static_assert(kA % 1024 == 0 && 2 * hd::kNP * 128 * 2 <= kA, "operand layout");
-static_assert(kBars % 8 == 0 && kCarry + kMaxGroups <= 80, "carry layout");
+static_assert(kBars % 8 == 0 && kCarry + kMaxGroups <= kCarryStride, "carry layout");
 static_assert(kAlloc <= 232448, "shared memory per block");
 }  // namespace hd3
 
@@ -2857,8 +2858,9 @@ __global__ void __launch_bounds__(hd3::kThreads, 1) head_fused_kernel(
     };
     const int w = rq * 32 + lane;                       // tile row = TMEM lane
     float* Zs = reinterpret_cast<float*>(smem + hd3::kZs + e * hd3::kZsBytes);
-    float* carry_mine = reinterpret_cast<float*>(smem + hd3::kCarryOff) + e * 80;
-    const float* carry_prev = reinterpret_cast<const float*>(smem + hd3::kCarryOff) + (e ^ 1) * 80;
+    float* carry_mine = reinterpret_cast<float*>(smem + hd3::kCarryOff) + e * hd3::kCarryStride;
+    const float* carry_prev =
+        reinterpret_cast<const float*>(smem + hd3::kCarryOff) + (e ^ 1) * hd3::kCarryStride;
     float* red = reinterpret_cast<float*>(smem + hd3::kRed) + e * 4 * kMaxGroups;
     Cursor ec;
     cur_init(ec);
