@@ -25,7 +25,8 @@ EXPORTED = (
     "chm_variant_workspace_bytes", "chm_variant",
     "chm_block_packed_bytes", "chm_pack_block", "chm_block_workspace_bytes",
     "chm_block_forward", "chm_forward_noalloc", "chm_noalloc_read_status", "chm_read_status",
-    "chm_last_launch_count", "chm_timing_enable", "chm_timing_collect",
+    "chm_selftest_wait_timeout", "chm_last_launch_count", "chm_timing_enable",
+    "chm_timing_collect",
 )
 TIMING_CLASSES = ("stem", "stats", "mlp", "profile_head", "count_head", "score", "other")
 
@@ -93,6 +94,7 @@ def _declare(lib):
         "chm_forward_noalloc": (i32, [desc_p, vp, i32, vp, i32, vp, vp, vp, vp]),
         "chm_read_status": (i32, [vp, vp]),
         "chm_noalloc_read_status": (i32, [vp]),
+        "chm_selftest_wait_timeout": (i32, [vp, sz, vp]),
         "chm_last_launch_count": (ctypes.c_int64, []),
         "chm_timing_enable": (None, [i32]),
         "chm_timing_collect": (i32, [ctypes.POINTER(ctypes.c_double),

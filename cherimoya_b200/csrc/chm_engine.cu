@@ -1212,6 +1212,16 @@ int32_t chm_read_status(void* workspace, chm_stream_t stream) {
   return s;
 }
 
+int32_t chm_selftest_wait_timeout(void* workspace, size_t workspace_bytes,
+                                  chm_stream_t stream) {
+  if (!workspace || workspace_bytes < sizeof(int) || !aligned(workspace, sizeof(int)))
+    return CHM_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(workspace, 0, sizeof(int), st) != cudaSuccess) return CHM_ERR_CUDA;
+  wait_timeout_selftest_kernel<<<1, 32, 0, st>>>(static_cast<int*>(workspace));
+  return launch_status();
+}
+
 int32_t chm_noalloc_read_status(chm_stream_t stream) {
   uint8_t* ws = nullptr;
   CHM_TRY(noalloc_scratch(&ws));

@@ -2997,6 +2997,25 @@ __global__ void __launch_bounds__(hd3::kThreads, 1) head_fused_kernel(
   }
 }
 
+// ============================================================== wait self-test
+// The bounded-wait path of every pipeline, exercised on purpose: thread 0
+// waits, with the pipelines' own abortable wait (2 s of wall time), on an
+// mbarrier that nothing arrives on, then records the timeout in the status
+// word as a stalled pipeline would. Nothing is in flight when it returns, so
+// the context stays usable.
+__global__ void wait_timeout_selftest_kernel(int* status) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    mbar_init_fence();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && !mbar_wait_abortable(&bar, 0, &abort_flag))
+    atomicExch(status, kStatusTimeout);
+}
+
 // ============================================================== scoring
 // Row-wise softmax of a reference profile flattened over (n_out, Lout), and
 // (pw != nullptr) the row's ProfileWrapper value

@@ -240,6 +240,15 @@ int32_t chm_noalloc_read_status(chm_stream_t stream);
  * the kernels of the last calls recorded in `workspace`. */
 int32_t chm_read_status(void* workspace, chm_stream_t stream);
 
+/* Self-test of the bounded device-side waits: launches one block whose
+ * thread waits, with the pipelines' abortable wait (about 2 s of wall time),
+ * on a barrier that nothing completes, and records the timeout in the status
+ * word at `workspace` (at least 4 bytes). chm_read_status(workspace, stream)
+ * then returns CHM_ERR_DEVICE_TIMEOUT; the context stays usable. No upstream
+ * counterpart. */
+int32_t chm_selftest_wait_timeout(void* workspace, size_t workspace_bytes,
+                                  chm_stream_t stream);
+
 /* Number of engine kernel launches the last chm_* call on this thread
  * issued (for the benchmark's launch accounting). */
 int64_t chm_last_launch_count(void);
