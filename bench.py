@@ -57,7 +57,10 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "seqs/sec fwd (2114bp, 9-layer) & ISM mutants/sec at 1/2/4/8 B200; % roofline"
-MLP_DRAM_BYTES_PER_SEQ = (138.766592e6 + 93.712896e6) / 256   # measured, bf16 mode
+# DRAM bytes (read + write) of one default-width MLP launch per sequence, bf16:
+# mean of the nine launches of one forward under ncu at batch 256
+# (profiles/mlp_ws_dram_all_layers_bf16_b256.md)
+MLP_DRAM_BYTES_PER_SEQ = 230.26e6 / 256
 L = 2114
 WORKLOADS = {
     # name: (model kwargs, default batch per GPU, input seed base, unit)
@@ -690,8 +693,8 @@ def run_ours(args, world, rank, local):
         "peak_source": "{} bf16_tflops (burst)".format(peak_src),
         "frac_of_sustained": achieved / peaks["bf16_tflops_sustained"],
         # DRAM bytes of one MLP launch of the default-width backbone: ncu
-        # dram__bytes_read.sum + write.sum of one launch at batch 256, scaled
-        # by the sequences processed (profiles/mlp_ws_kernel_bf16_b256.md)
+        # dram__bytes_read.sum + write.sum averaged over the nine launches of
+        # a forward at batch 256, scaled by the sequences processed
         "traffic": (MLP_DRAM_BYTES_PER_SEQ * args.batch
                     if args.mode == "bf16" and default_width and not variant else None),
         "traffic_unit": "bytes per launch",
