@@ -412,19 +412,21 @@ int launch_stats(const Dims& m, const act_t* X, const float* convw, int dil, int
     }
     const int n_kb = (K + kS - 1) / kS;
     LaunchTimer timer(kKStats, st);
-    auto go = [&](auto kern) {
-      launch_k(pdl, kern, dim3(batch), dim3(kStatsChainThreads), 0, st,
+    auto go = [&](auto kern, uint32_t smem) {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem));
+      launch_k(pdl, kern, dim3(batch), dim3(kStatsChainThreads), smem, st,
                reinterpret_cast<const __nv_bfloat16*>(X), convw, dil, m.L, m.C, n_kb, 1e-3f,
                stats);
     };
     auto pick = [&](auto cp) {
       constexpr int CPc = decltype(cp)::value;
       switch (kS) {
-        case 4: go(stats_chain_kernel<CPc, 4>); break;
-        case 6: go(stats_chain_kernel<CPc, 6>); break;
-        case 8: go(stats_chain_kernel<CPc, 8>); break;
-        case 9: go(stats_chain_kernel<CPc, 9>); break;
-        default: go(stats_chain_kernel<CPc, 12>); break;
+        case 4: go(stats_async_kernel<CPc, 4>, stats_async_smem_bytes<4>()); break;
+        case 6: go(stats_async_kernel<CPc, 6>, stats_async_smem_bytes<6>()); break;
+        case 8: go(stats_async_kernel<CPc, 8>, stats_async_smem_bytes<8>()); break;
+        case 9: go(stats_async_kernel<CPc, 9>, stats_async_smem_bytes<9>()); break;
+        default: go(stats_async_kernel<CPc, 12>, stats_async_smem_bytes<12>()); break;
       }
     };
     if (m.CP == 64) {

@@ -836,6 +836,130 @@ __global__ void __launch_bounds__(kStatsChainThreads, 2) stats_chain_kernel(
   }
 }
 
+// The same statistics, with each thread's segment rows brought into shared
+// memory by cp.async, double-buffered: the rows of the thread's next segment
+// are in flight while it computes the current one, so the bytes in flight
+// per SM are no longer bounded by registers (2 x (kS + 2) x 16 B per thread,
+// two blocks per SM). Each thread reads back only the slots it filled itself,
+// so no block barrier is needed; slots are interleaved across threads
+// (conflict-free 16-byte reads). Arithmetic and reduction order are those of
+// stats_chain_kernel.
+template <int kS>
+constexpr uint32_t stats_async_smem_bytes() {
+  return static_cast<uint32_t>(2 * (kS + 2) * kStatsChainThreads * 16);
+}
+
+template <int CP, int kS>
+__global__ void __launch_bounds__(kStatsChainThreads, 2) stats_async_kernel(
+    const __nv_bfloat16* __restrict__ X, const float* __restrict__ convw, int dil, int L, int C,
+    int n_kb, float eps, float2* __restrict__ stats) {
+  constexpr int kCh = CP / 8;                       // 16-byte chunks per row
+  static_assert(kStatsChainThreads % kCh == 0, "chunk count must divide the block");
+  constexpr int kSegStride = kStatsChainThreads / kCh;
+  constexpr int kRows = kS + 2;
+  extern __shared__ uint4 slots[];                  // [buf][row][thread]
+  __shared__ double red[2][kStatsChainThreads / 32];
+  const int b = blockIdx.x, tid = threadIdx.x;
+  const int ch = tid % kCh;
+  f2 w0[4], w1[4], w2[4];
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    const int c = ch * 8 + 2 * m;
+    w0[m] = f2{c < C ? convw[c] : 0.f, c + 1 < C ? convw[c + 1] : 0.f};
+    w1[m] = f2{c < C ? convw[CP + c] : 0.f, c + 1 < C ? convw[CP + c + 1] : 0.f};
+    w2[m] = f2{c < C ? convw[2 * CP + c] : 0.f, c + 1 < C ? convw[2 * CP + c + 1] : 0.f};
+  }
+  griddep_wait();                          // the previous kernel's outputs are visible
+  const uint4* Xb = reinterpret_cast<const uint4*>(X + (size_t)b * L * CP) + ch;
+  const int n_seg = dil * n_kb;
+  auto r0_of = [&](int seg) {                       // chain position k0 = kb * kS
+    const int kb = seg / dil;
+    return (seg - kb * dil) + kb * kS * dil;
+  };
+  auto fetch = [&](int seg, int buf) {              // rows r0 + (j - 1) * d
+    const int r0 = r0_of(seg);
+#pragma unroll
+    for (int j = 0; j < kRows; ++j) {
+      const int r = r0 + (j - 1) * dil;
+      const bool v = r >= 0 && r < L;
+      cp_async16(&slots[(buf * kRows + j) * kStatsChainThreads + tid], Xb + (size_t)(v ? r : 0) * kCh,
+                 v);
+    }
+    cp_async_commit();
+  };
+  double S = 0.0, Q = 0.0;
+  int seg = tid / kCh, buf = 0;
+  if (seg < n_seg) fetch(seg, 0);
+  for (; seg < n_seg; seg += kSegStride, buf ^= 1) {
+    const int nxt = seg + kSegStride;
+    if (nxt < n_seg) {
+      fetch(nxt, buf ^ 1);
+      cp_async_wait<1>();                           // this segment's rows have landed
+    } else {
+      cp_async_wait<0>();
+    }
+    const int r0 = r0_of(seg);
+    const uint4* sv = &slots[buf * kRows * kStatsChainThreads + tid];
+    uint4 vl = sv[0], vc = sv[kStatsChainThreads];
+    f2 sy[4], sq[4];
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      sy[m] = f2{0.f, 0.f};
+      sq[m] = f2{0.f, 0.f};
+    }
+#pragma unroll
+    for (int j = 1; j <= kS; ++j) {
+      const uint4 vr = sv[(j + 1) * kStatsChainThreads];
+      if (r0 + (j - 1) * dil < L) {
+        const uint32_t* pl = reinterpret_cast<const uint32_t*>(&vl);
+        const uint32_t* pc = reinterpret_cast<const uint32_t*>(&vc);
+        const uint32_t* pr = reinterpret_cast<const uint32_t*>(&vr);
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          const f2 xl{__uint_as_float(pl[m] << 16), __uint_as_float(pl[m] & 0xFFFF0000u)};
+          const f2 xc{__uint_as_float(pc[m] << 16), __uint_as_float(pc[m] & 0xFFFF0000u)};
+          const f2 xr{__uint_as_float(pr[m] << 16), __uint_as_float(pr[m] & 0xFFFF0000u)};
+          const f2 y = fma2(w0[m], xl, fma2(w1[m], xc, mul2(w2[m], xr)));
+          sy[m] = f2{sy[m].x + y.x, sy[m].y + y.y};
+          sq[m] = fma2(y, y, sq[m]);
+        }
+      }
+      vl = vc;
+      vc = vr;
+    }
+    const float ts = ((sy[0].x + sy[0].y) + (sy[1].x + sy[1].y)) +
+                     ((sy[2].x + sy[2].y) + (sy[3].x + sy[3].y));
+    const float tq = ((sq[0].x + sq[0].y) + (sq[1].x + sq[1].y)) +
+                     ((sq[2].x + sq[2].y) + (sq[3].x + sq[3].y));
+    S += static_cast<double>(ts);
+    Q += static_cast<double>(tq);
+  }
+  const int warp = tid >> 5, lane = tid & 31;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    S += __shfl_xor_sync(0xffffffffu, S, o);
+    Q += __shfl_xor_sync(0xffffffffu, Q, o);
+  }
+  if (lane == 0) {
+    red[0][warp] = S;
+    red[1][warp] = Q;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    double ss = 0.0, qq = 0.0;
+    for (int i = 0; i < kStatsChainThreads / 32; ++i) {
+      ss += red[0][i];
+      qq += red[1][i];
+    }
+    const double n = static_cast<double>(L) * static_cast<double>(C);
+    const double mean = ss / n;
+    double var = qq / n - mean * mean;
+    if (var < 0.0) var = 0.0;
+    stats[b] = make_float2(static_cast<float>(mean),
+                           static_cast<float>(1.0 / sqrt(var + static_cast<double>(eps))));
+  }
+}
+
 // ============================================================== MLP
 // One Cheri Block update for 128-row tiles of the flattened (B*L) rows:
 //   A1 = bf16((conv(X) - mean) * rstd)            (built by all threads)

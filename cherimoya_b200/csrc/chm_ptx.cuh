@@ -124,6 +124,22 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int x, 
       : "memory");
 }
 
+// 16-byte asynchronous copy global -> shared (L2 only); with `valid` false
+// the destination is zero-filled and nothing is read.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+// wait until at most N committed groups of this thread are still in flight
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // 2-D tiled TMA store from this CTA's shared memory (bulk async group).
 __device__ __forceinline__ void tma_store_2d(const void* tmap, const void* src, int x, int y) {
   asm volatile(
