@@ -646,7 +646,7 @@ __global__ void __launch_bounds__(sm2::kThreads, 1) stem_tc_kernel(
 // Per-example LayerNorm statistics of the dilated depthwise conv output
 // y = w0 x[l-d] + w1 x[l] + w2 x[l+d] over the (L, C) plane (upstream
 // cheri.py:84-98), any activation type, one block per example (the fp32
-// path; bf16 activations use stats_chain_kernel below). Lanes read 8
+// path; bf16 activations use stats_async_kernel below). Lanes read 8
 // channels (16 B bf16 / 32 B fp32); CP/8 lanes cover one row, so a warp
 // covers 256/CP rows per load instruction. Each thread accumulates sum(y) and sum(y^2)
 // of one row's 8 channels in fp32 and adds them into fp64 accumulators; the
@@ -738,112 +738,20 @@ __global__ void __launch_bounds__(kStats2Threads) stats_example_kernel(
 // of an example belongs to the chain r = rho + k*d (rho < d); a segment is kS
 // consecutive chain positions k0 .. k0+kS-1 of one chain for one 8-channel
 // chunk, so the conv's left / centre / right operands of chain position k are
-// positions k-1, k, k+1 of the same chain: the thread loads the segment plus
+// positions k-1, k, k+1 of the same chain: the thread fetches the segment plus
 // one halo row on each side (16 B per row, a warp covers whole rows of
-// adjacent chains) and slides a three-row window through registers. The conv
-// is fp32 on paired lanes (same arithmetic as the MLP producer); each
-// segment's fp32 sums of y and y^2 fold into fp64 accumulators, and the block
-// reduction is fp64 in a fixed order (deterministic; var = E[y^2] - mean^2
-// without catastrophic cancellation).
+// adjacent chains) and slides a three-row window through them. The rows come
+// into shared memory by cp.async, double-buffered per thread: the rows of the
+// thread's next segment are in flight while it sums the current one, so the
+// bytes in flight per SM are not bounded by registers (2 x (kS + 2) x 16 B per
+// thread, two blocks per SM). Each thread reads back only the slots it filled
+// itself, so no block barrier is needed; slots are interleaved across threads
+// (conflict-free 16-byte reads). The conv is fp32 on paired lanes (same
+// arithmetic as the MLP producer); each segment's fp32 sums of y and y^2 fold
+// into fp64 accumulators, and the block reduction is fp64 in a fixed order
+// (deterministic; var = E[y^2] - mean^2 without catastrophic cancellation).
 constexpr int kStatsChainThreads = 256;
 
-template <int CP, int kS>
-__global__ void __launch_bounds__(kStatsChainThreads, 2) stats_chain_kernel(
-    const __nv_bfloat16* __restrict__ X, const float* __restrict__ convw, int dil, int L, int C,
-    int n_kb, float eps, float2* __restrict__ stats) {
-  constexpr int kCh = CP / 8;                       // 16-byte chunks per row
-  static_assert(kStatsChainThreads % kCh == 0, "chunk count must divide the block");
-  constexpr int kSegStride = kStatsChainThreads / kCh;
-  __shared__ double red[2][kStatsChainThreads / 32];
-  const int b = blockIdx.x, tid = threadIdx.x;
-  const int ch = tid % kCh;
-  f2 w0[4], w1[4], w2[4];
-#pragma unroll
-  for (int m = 0; m < 4; ++m) {
-    const int c = ch * 8 + 2 * m;
-    w0[m] = f2{c < C ? convw[c] : 0.f, c + 1 < C ? convw[c + 1] : 0.f};
-    w1[m] = f2{c < C ? convw[CP + c] : 0.f, c + 1 < C ? convw[CP + c + 1] : 0.f};
-    w2[m] = f2{c < C ? convw[2 * CP + c] : 0.f, c + 1 < C ? convw[2 * CP + c + 1] : 0.f};
-  }
-  griddep_wait();                          // the previous kernel's outputs are visible
-  const uint4* Xb = reinterpret_cast<const uint4*>(X + (size_t)b * L * CP) + ch;
-  const int n_seg = dil * n_kb;
-  double S = 0.0, Q = 0.0;
-  for (int seg = tid / kCh; seg < n_seg; seg += kSegStride) {
-    const int kb = seg / dil;
-    const int rho = seg - kb * dil;
-    const int r0 = rho + kb * kS * dil;             // chain position k0 = kb * kS
-    if (r0 >= L) continue;
-    uint4 v[kS + 2];                                // rows r0 + (j - 1) * d
-#pragma unroll
-    for (int j = 0; j < kS + 2; ++j) {
-      const int r = r0 + (j - 1) * dil;
-      v[j] = (r >= 0 && r < L) ? __ldg(Xb + (size_t)r * kCh) : make_uint4(0u, 0u, 0u, 0u);
-    }
-    f2 sy[4], sq[4];
-#pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      sy[m] = f2{0.f, 0.f};
-      sq[m] = f2{0.f, 0.f};
-    }
-#pragma unroll
-    for (int j = 1; j <= kS; ++j) {
-      if (r0 + (j - 1) * dil < L) {
-        const uint32_t* pl = reinterpret_cast<const uint32_t*>(&v[j - 1]);
-        const uint32_t* pc = reinterpret_cast<const uint32_t*>(&v[j]);
-        const uint32_t* pr = reinterpret_cast<const uint32_t*>(&v[j + 1]);
-#pragma unroll
-        for (int m = 0; m < 4; ++m) {
-          const f2 xl{__uint_as_float(pl[m] << 16), __uint_as_float(pl[m] & 0xFFFF0000u)};
-          const f2 xc{__uint_as_float(pc[m] << 16), __uint_as_float(pc[m] & 0xFFFF0000u)};
-          const f2 xr{__uint_as_float(pr[m] << 16), __uint_as_float(pr[m] & 0xFFFF0000u)};
-          const f2 y = fma2(w0[m], xl, fma2(w1[m], xc, mul2(w2[m], xr)));
-          sy[m] = f2{sy[m].x + y.x, sy[m].y + y.y};
-          sq[m] = fma2(y, y, sq[m]);
-        }
-      }
-    }
-    const float ts = ((sy[0].x + sy[0].y) + (sy[1].x + sy[1].y)) +
-                     ((sy[2].x + sy[2].y) + (sy[3].x + sy[3].y));
-    const float tq = ((sq[0].x + sq[0].y) + (sq[1].x + sq[1].y)) +
-                     ((sq[2].x + sq[2].y) + (sq[3].x + sq[3].y));
-    S += static_cast<double>(ts);
-    Q += static_cast<double>(tq);
-  }
-  const int warp = tid >> 5, lane = tid & 31;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    S += __shfl_xor_sync(0xffffffffu, S, o);
-    Q += __shfl_xor_sync(0xffffffffu, Q, o);
-  }
-  if (lane == 0) {
-    red[0][warp] = S;
-    red[1][warp] = Q;
-  }
-  __syncthreads();
-  if (tid == 0) {
-    double ss = 0.0, qq = 0.0;
-    for (int i = 0; i < kStatsChainThreads / 32; ++i) {
-      ss += red[0][i];
-      qq += red[1][i];
-    }
-    const double n = static_cast<double>(L) * static_cast<double>(C);
-    const double mean = ss / n;
-    double var = qq / n - mean * mean;
-    if (var < 0.0) var = 0.0;
-    stats[b] = make_float2(static_cast<float>(mean),
-                           static_cast<float>(1.0 / sqrt(var + static_cast<double>(eps))));
-  }
-}
-
-// The same statistics, with each thread's segment rows brought into shared
-// memory by cp.async, double-buffered: the rows of the thread's next segment
-// are in flight while it computes the current one, so the bytes in flight
-// per SM are no longer bounded by registers (2 x (kS + 2) x 16 B per thread,
-// two blocks per SM). Each thread reads back only the slots it filled itself,
-// so no block barrier is needed; slots are interleaved across threads
-// (conflict-free 16-byte reads). Arithmetic and reduction order are those of
-// stats_chain_kernel.
 template <int kS>
 constexpr uint32_t stats_async_smem_bytes() {
   return static_cast<uint32_t>(2 * (kS + 2) * kStatsChainThreads * 16);
